@@ -1,0 +1,387 @@
+"""Benchmark of the mxtorch hot path on B200.
+
+Headline: int8d x int8d packed GEMM, M=N=K=4096,
+block 128, seeded N(0,1) fp32 operands quantized on the device; output int16d
+(requantized, packed).  At N GPUs the weight B is column-sharded and the
+output all-gathered (strong scaling: the total work is fixed).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `value` times the GEMM on operands already
+resident in HBM; `e2e` times the user-facing call with host buffers (h2d of
+the fp32 operands, quantize, matmul, d2h of the packed result).  Extra
+sub-results (weight-only int4d GEMM / GEMV, quantize) go under `extra`.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M = N = K = 4096
+BLOCK = 128
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.p is not None:
+            time.sleep(0.2)
+            self.p.terminate()
+            try:
+                out, _ = self.p.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+                out, _ = self.p.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def time_steps(fn, steps, flush, stream=None):
+    """Device time of each call (CUDA events on the launching stream); L2
+    flushed before each timed call."""
+    st = stream or torch.cuda.current_stream()
+    ts = []
+    for _ in range(steps):
+        flush()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        fn()
+        e1.record(st)
+        ts.append((e0, e1))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ts]
+
+
+def dist_setup(gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_inputs():
+    torch.manual_seed(0)
+    a = torch.randn(M, K)
+    b = torch.randn(K, N)
+    return a, b
+
+
+# ── reference arm: the CPU oracle port on the host cores ─────────────────────
+def cpu_baseline_sample(rows=256, reps=1):
+    """Reference path on the host: quantize A-rows + B, packed int GEMM, requant
+    (oracle port of mxtorch.py:1426-1463, 1299-1385) on a row sample of A."""
+    from oracle import mx_oracle as O
+    a, b = make_inputs()
+    a = a[:rows].numpy()
+    b = b.numpy()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        pa, sa, _ = O.quantize(a, 8, "int", BLOCK)
+        pb, sb, _ = O.quantize(b, 8, "int", BLOCK)
+        ca = O.unpack(pa, 8, a.size)
+        cb = O.unpack(pb, 8, b.size)
+        O.qscale_matmul(ca, sa, cb, sb, rows, K, N, BLOCK, 16)
+        ts.append(time.perf_counter() - t0)
+    t = min(ts)
+    return 2.0 * rows * N * K / t / 1e12, t
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = 128
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, t = cpu_baseline_sample(rows)
+        if i >= args.warmup:
+            vals.append(v)
+    v = statistics.median(vals)
+    cores = os.cpu_count()
+    line = {
+        "metric": "int8d x int8d packed GEMM throughput (4096^3, block 128)",
+        "value": v, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong", "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "int8d x int8d GEMM M=N=K=4096 block 128 (configs[1])",
+                   "sample": f"{rows} rows of A x full B per step"},
+        "cpu_baseline": {"value": v, "unit": "TOPS", "cores": cores, "kind": "port",
+                         "sample": f"quantize {rows}x4096 A + 4096x4096 B, GEMM, requant"},
+        "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "vs_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ── our arm ──────────────────────────────────────────────────────────────────
+def run_ours(args, world, rank, local):
+    import qtpytorch_b200 as mxb
+    from qtpytorch_b200 import _lib as L
+    from qtpytorch_b200 import ops
+    from qtpytorch_b200.parallel import ShardedQGemmWeight, sharded_qgemm
+
+    dev = torch.device("cuda", local)
+    lib = L.load()
+    hbm, bf16, bf16s, peak_src = peaks()
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+
+    a_h, b_h = make_inputs()
+    qa = mxb.mx_tensor.quantize(a_h.to(dev), mxb.int8d, BLOCK)
+    qb = mxb.mx_tensor.quantize(b_h.to(dev), mxb.int8d, BLOCK)
+    w = ShardedQGemmWeight(qb, world, rank)
+    nl = w.n1 - w.n0
+
+    def step():
+        return sharded_qgemm(qa, w)
+
+    # GEMM kernel alone (fp32 C, no requantization) for the roofline
+    c32 = torch.empty(M, nl, dtype=torch.float32, device=dev)
+    wsb = lib.mxb_qgemm_workspace_size(M, K, nl, 8, BLOCK)
+    ws = L.workspace(wsb, dev)
+    cp = torch.empty(lib.mxb_packed_bytes(M * nl, 16, BLOCK) // 4, dtype=torch.int32, device=dev)
+    cs = torch.empty(M * nl // BLOCK, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def gemm_only():
+        rc = lib.mxb_qgemm(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales), qa._mx_scales.numel(),
+                           L.ptr(w.codes), L.ptr(w.scales), w.scales.numel(), M, K, nl, 8,
+                           BLOCK, 32, L.ptr(cp), L.ptr(cs), L.ptr(c32), L.ptr(ws), wsb,
+                           stream.cuda_stream)
+        L.check(rc, "mxb_qgemm")
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+        gemm_only()
+    barrier(world)
+
+    n0 = lib.mxb_launch_count()
+    with Clocks(local) as clk:
+        barrier(world)
+        ts = time_steps(step, args.steps, flush, stream)
+        barrier(world)
+    launches = (lib.mxb_launch_count() - n0) // max(args.steps, 1) * args.steps
+    step_ms = max_over_ranks(sum(ts) / len(ts), world)
+    value = 2.0 * M * N * K / (step_ms * 1e-3) / 1e12
+
+    tg = time_steps(gemm_only, args.steps, flush, stream)
+    gemm_ms = max_over_ranks(sum(tg) / len(tg), world)
+    int8_peak = 2.0 * bf16  # kind::i8 issues twice the bf16 rate on sm_100
+    achieved = 2.0 * M * nl * K / (gemm_ms * 1e-3) / 1e12
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        traffic = json.load(open(tf)).get("qgemm_int8_4096", None)
+
+    # e2e: host fp32 operands -> public API -> host packed result
+    a_pin = a_h.pin_memory()
+    b_pin = b_h.pin_memory()
+
+    def e2e_step():
+        xa = a_pin.to(dev, non_blocking=True)
+        xb = b_pin.to(dev, non_blocking=True)
+        ea = mxb.mx_tensor.quantize(xa, mxb.int8d, BLOCK)
+        eb = mxb.mx_tensor.quantize(xb, mxb.int8d, BLOCK)
+        ec = sharded_qgemm(ea, ShardedQGemmWeight(eb, world, rank))
+        return ec._mx_packed.to("cpu"), ec._mx_scales.to("cpu")
+
+    for _ in range(2):
+        e2e_step()
+    barrier(world)
+    te = []
+    for _ in range(args.steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        pk, sc = e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        te.append(e0.elapsed_time(e1))
+    e2e_ms = max_over_ranks(sum(te) / len(te), world)
+    h2d = a_h.numel() * 4 + b_h.numel() * 4
+    d2h = pk.numel() * pk.element_size() + sc.numel() * 4
+
+    extra = {}
+    if world == 1 and not args.no_extra:
+        extra = run_extras(args, dev, flush, stream, hbm, bf16)
+
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            torch.set_num_threads(os.cpu_count() or 1)
+            v_cpu, t_cpu = cpu_baseline_sample(128)
+            cpu = {"value": v_cpu, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port",
+                   "sample": "quantize 128x4096 A rows + 4096x4096 B, int GEMM, requant "
+                             f"({t_cpu:.2f} s)"}
+        line = {
+            "metric": "int8d x int8d packed GEMM throughput (4096^3, block 128)",
+            "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "int8d x int8d GEMM M=N=K=4096 block 128 -> int16d "
+                                   "(configs[1])",
+                       "global_batch": M, "parallelism": f"N-sharded x{world}",
+                       "l2": "flushed (256 MiB write) before every timed step"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak,
+                         "unit": "TOPS", "frac": achieved / int8_peak, "traffic": traffic,
+                         "kernel": "qgemm (fp32 C, before requantization)",
+                         "peak_note": f"2x {peak_src} bf16 burst {bf16} TFLOP/s"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": 2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "extra": extra,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_extras(args, dev, flush, stream, hbm, bf16):
+    """Weight-only int4d and quantize/pack sub-results."""
+    import qtpytorch_b200 as mxb
+    from qtpytorch_b200 import ops
+    out = {}
+    steps = max(3, min(args.steps, 10))
+    g = torch.Generator().manual_seed(1)
+    W = torch.randn(11008, 4096, generator=g) * 0.02
+    lin = torch.nn.Linear(4096, 11008, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(W)
+    ml = mxb.mx_linear.from_linear(lin.to(dev), mxb.int4d, 128)
+    wbytes = ml._mx_weight._mx_packed.numel() + ml._mx_weight._mx_scales.numel() * 4
+    g2 = torch.Generator().manual_seed(2)
+    for Mx in (1, 16, 128, 2048):
+        x = torch.randn(Mx, 4096, generator=g2).bfloat16().to(dev)
+        for _ in range(3):
+            ml(x)
+        t = statistics.median(time_steps(lambda: ml(x), steps, flush, stream))
+        flops = 2.0 * Mx * 4096 * 11008
+        byts = wbytes + x.numel() * 2 + Mx * 11008 * 4
+        out[f"wonly_int4d_M{Mx}"] = {"ms": t, "tflops": flops / t / 1e9,
+                                     "gbs": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / hbm,
+                                     "tensor_frac_bf16": flops / t / 1e9 / bf16}
+    for dt, n in (("int2d", 1 << 28), ("int4d", 1 << 28), ("float4d", 1 << 26)):
+        x = torch.randn(n, device=dev)
+        d = mxb.get_mx_dtype(dt)
+        for _ in range(2):
+            ops.quantize(x, d, 128)
+        t = statistics.median(time_steps(lambda: ops.quantize(x, d, 128), steps, flush, stream))
+        byts = n * 4 + n * d.bits / 8 + n / 128 * 4
+        out[f"quantize_{dt}_fp32_2^{n.bit_length() - 1}"] = {
+            "ms": t, "gbs": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / hbm}
+        del x
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extra", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    run_ours(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

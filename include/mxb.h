@@ -1,0 +1,160 @@
+/*
+ * mxb — B200 (sm_100a) kernels for the mxtorch quantize / pack / packed-matmul
+ * hot path, behind a C ABI.
+ *
+ * Every entry point takes plain device pointers and sizes, runs on the CUDA
+ * stream passed as `stream` (a cudaStream_t, or NULL for the legacy default
+ * stream), returns an int status (MXB_OK or a negative MXB_E_* code, never
+ * aborts) and allocates no device memory: the caller owns every buffer,
+ * including the workspaces whose sizes the *_workspace_size functions report.
+ * Calls are stateless and may run concurrently on different streams.
+ *
+ * Data layout (the reference's storage contract, mxtorch.py:870-985,
+ * 1426-1528): a tensor of n elements is flattened row-major, zero-padded to
+ * nb = ceil(n / block) blocks of `block` elements, and each block gets one
+ * fp32 scale.  Codes are packed LSB-first as two's complement: 8/bits codes
+ * per byte for bits in {1, 2, 4, 8}; 16-bit codes go two per int32 word, low
+ * half first.  The packed buffer holds nb * block codes (padding included).
+ * float4 ("float4d") codes are 4-bit indices into the sorted 16-entry grid
+ * {±0, ±1/12, ±1/6, ±1/4, ±1/3, ±1/2, ±2/3, ±1}.
+ */
+#ifndef MXB_H_
+#define MXB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define MXB_OK 0
+#define MXB_E_SHAPE (-1)     /* unsupported or inconsistent sizes */
+#define MXB_E_DTYPE (-2)     /* unsupported bits / kind / variant combination */
+#define MXB_E_ALIGN (-3)     /* a pointer is not aligned as the call requires */
+#define MXB_E_CUDA (-4)      /* a CUDA runtime call or launch failed */
+#define MXB_E_ARG (-6)       /* null pointer or invalid enum */
+#define MXB_E_WORKSPACE (-7) /* workspace missing or too small */
+
+/* input element types */
+#define MXB_F32 0
+#define MXB_BF16 1
+
+/* code kinds */
+#define MXB_KIND_INT 0   /* absmax integer codes (intNd) */
+#define MXB_KIND_FLOAT 1 /* float4 grid-index codes (float4d) */
+
+/* variants */
+#define MXB_VAR_BASE 0
+#define MXB_VAR_H 1 /* randomized Hadamard rotation of the last dim before quantizing */
+
+/* weight-only matmul precision modes */
+#define MXB_MODE_PARITY 0 /* fp32-faithful: |y - y_ref| <= 1e-5 * (|x| @ |W|) */
+#define MXB_MODE_FAST 1   /* weights rounded to bf16 once: ~4e-3 relative per weight */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int mxb_version(void);
+
+/* Text of the last CUDA error seen by this thread ("" if none). */
+const char* mxb_last_error(void);
+
+/* Number of kernels this library has launched in this process (all threads). */
+uint64_t mxb_launch_count(void);
+
+/* Bytes of packed storage for n codes of `bits` (1,2,4,8,16) at `block`. */
+size_t mxb_packed_bytes(int64_t n, int bits, int block);
+
+/* Workspace bytes mxb_quantize needs for these arguments (0 for the common
+ * vectorised cases). */
+size_t mxb_quantize_workspace_size(int64_t n, int64_t row_len, int bits, int kind,
+                                   int variant, int block);
+
+/*
+ * Block-wise absmax quantize + bit-pack.
+ * Replaces mxtorch `quantize` (mxtorch.py:1684-1763) for the base and "h"
+ * variants, i.e. `_quant_int` (1426-1463), `_quant_float` (1465-1528),
+ * `bit_packer.pack_auto` (976-980) and, for "h", `hadamard_rotation.rotate`
+ * (2866-2890) along rows of `row_len` elements.
+ *   x        device, n elements of x_dtype (MXB_F32 / MXB_BF16), row-major
+ *   row_len  length of the last dim (the rotated dim for "h"; n for 1-D)
+ *   bits     1, 2, 4 or 8 (kind INT) / 4 (kind FLOAT)
+ *   signs    "h" only: pow2ceil(row_len) fp32 ±1 values
+ *   packed   mxb_packed_bytes(n, bits, block) bytes
+ *   scales   ceil(n / block) floats
+ * Codes and scales are bit-identical to the reference's CPU path.
+ */
+int mxb_quantize(const void* x, int x_dtype, int64_t n, int64_t row_len, int bits,
+                 int kind, int variant, int block, const float* signs, void* packed,
+                 float* scales, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Unpack + dequantize to fp32.
+ * Replaces mxtorch `_dequant` (mxtorch.py:1530-1597).  bits may also be 16
+ * (the int16d output of the int8 x int8 matmul).  For "h" the inverse
+ * rotation (`hadamard_rotation.unrotate`, 2892-2904) runs along rows of
+ * `row_len`, the dimension quantize rotated.
+ *   out      n floats
+ */
+int mxb_dequantize(const void* packed, const float* scales, int64_t n, int64_t row_len,
+                   int bits, int kind, int variant, int block, const float* signs,
+                   float* out, void* stream);
+
+/* Randomized Hadamard transform of `rows` rows of length d (pow2ceil(d) <=
+ * 32768), out-of-place or in place.  inverse=0: y = WHT(x * signs) / sqrt(n)
+ * (hadamard_rotation.rotate, mxtorch.py:2866-2890); inverse=1:
+ * y = WHT(x) / sqrt(n) * signs (unrotate, 2892-2904). */
+int mxb_hadamard_rows(const float* x, int64_t rows, int64_t d, const float* signs,
+                      int inverse, float* out, void* stream);
+
+/* Workspace bytes for mxb_qgemm. */
+size_t mxb_qgemm_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int block);
+
+/*
+ * Packed integer matmul C = A @ B of two quantized matrices, requantized.
+ * Replaces `_dispatch_qgemm` (mxtorch.py:5497-5573) -> `_qscale_matmul`
+ * (1299-1385) + `bit_packer.pack_auto`.
+ *   a_packed / a_scales  A [M, K], `bits` codes, a_nscales = ceil(M*K/block)
+ *   b_packed / b_scales  B [K, N], b_nscales = ceil(K*N/block)
+ * Per K-block kb: P = A[:, kb] @ B[kb, :] in exact integers, then
+ * C = C + fl(fl(P * sa[m, kb]) * sb[kb, n]) in kb order, sa = a_scales viewed
+ * [M, K/block] and sb = b_scales viewed [K/block, N] (the reference's layout;
+ * all-ones when the scale count does not match that view).  C is then
+ * requantized over flat blocks of `block` to `out_bits` codes
+ * (cs = max(amax, 1e-12) / max_out, code = rint(clamp(C / cs))).
+ *   out_bits  2, 4, 8 or 16 (the reference's choice: a.bits + b.bits), or 32
+ *             for the fp32 C alone (no requantization; c_packed / c_scales unused)
+ *   c_packed  mxb_packed_bytes(M*N, out_bits, block) bytes
+ *   c_scales  ceil(M*N/block) floats
+ *   c_f32     optional [M, N] fp32 C before requantization (may be NULL)
+ */
+int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
+              const void* b_packed, const float* b_scales, int64_t b_nscales, int64_t M,
+              int64_t K, int64_t N, int bits, int block, int out_bits, void* c_packed,
+              float* c_scales, float* c_f32, void* workspace, size_t workspace_bytes,
+              void* stream);
+
+/* Workspace bytes for mxb_linear_wonly. */
+size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits,
+                                       int kind, int block, int mode);
+
+/*
+ * Weight-only linear y = x @ dequant(W^T), fp32 output.
+ * Replaces `mx_linear.forward` (mxtorch.py:7454-7473): the weight is stored
+ * transposed, W^T [K = in, N = out], quantized flat (scale s[k, n // block]
+ * when N % block == 0), and y = fp32(x) @ fl(code * s).
+ *   x        [M, K] of x_dtype (MXB_F32 / MXB_BF16)
+ *   w_packed / w_scales  the mx_tensor storage of W^T
+ *   y        [M, N] fp32
+ * M <= 16 runs a split-K GEMV on the CUDA cores; larger M the tcgen05 GEMM.
+ */
+int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const void* w_packed,
+                     const float* w_scales, int64_t N, int bits, int kind, int block,
+                     int mode, float* y, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXB_H_ */

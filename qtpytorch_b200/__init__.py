@@ -1,0 +1,18 @@
+"""qtpytorch_b200 — B200-native (sm_100a) MX quantize / pack / packed matmul.
+
+The reference's hot-path API (DHDev0/qtpytorch ``mxtorch``) on CUDA kernels:
+``mx_tensor.quantize`` / ``dequantize`` / ``@``, ``mx_linear``, ``to_mx``,
+``mx_matmul``, ``get_mx_dtype``, ``register_kernel``.
+"""
+from .dtypes import (  # noqa: F401
+    _DTYPE_REGISTRY,
+    get_mx_dtype,
+    mx_dtype,
+    optimal_output_dtype,
+)
+from .dtypes import *  # noqa: F401,F403  (int4d, float4d, int8dh, ...)
+from .hadamard import sign_vector  # noqa: F401
+from .linear import mx_linear, to_mx  # noqa: F401
+from .tensor import mx_matmul, mx_tensor, register_kernel  # noqa: F401
+
+__version__ = "0.1.0"

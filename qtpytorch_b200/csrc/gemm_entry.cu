@@ -1,0 +1,100 @@
+// C-ABI entry points of the matmuls: routing between the tcgen05 kernels,
+// the split-K GEMV and the general-shape CUDA-core kernels.
+#include "mxb_common.cuh"
+#include "mxb_internal.h"
+
+using namespace mxb;
+
+namespace {
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+
+bool int_bits(int bits) { return bits == 1 || bits == 2 || bits == 4 || bits == 8; }
+// 32: fp32 C only (no requantization; c_f32 required)
+bool out_bits_ok(int bits) {
+  return bits == 2 || bits == 4 || bits == 8 || bits == 16 || bits == 32;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t mxb_qgemm_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int block) {
+  if (M <= 0 || K <= 0 || N <= 0 || block <= 0) return 0;
+  return align_up((size_t)M * N * sizeof(float)) + align_up(tc_qgemm_workspace(M, K, N, bits)) +
+         align_up(mxb_requant_workspace_size(M * N, block));
+}
+
+int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
+              const void* b_packed, const float* b_scales, int64_t b_nscales, int64_t M,
+              int64_t K, int64_t N, int bits, int block, int out_bits, void* c_packed,
+              float* c_scales, float* c_f32, void* workspace, size_t workspace_bytes,
+              void* stream) {
+  if (!int_bits(bits) || !out_bits_ok(out_bits)) return MXB_E_DTYPE;
+  if (M <= 0 || K <= 0 || N <= 0 || block <= 0) return MXB_E_SHAPE;
+  if (M * K >= (int64_t)1 << 31 || K * N >= (int64_t)1 << 31 || M * N >= (int64_t)1 << 31)
+    return MXB_E_SHAPE;
+  if (!a_packed || !a_scales || !b_packed || !b_scales) return MXB_E_ARG;
+  if (out_bits == 32 ? c_f32 == nullptr : (!c_packed || !c_scales)) return MXB_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t kbn = cdiv(K, block);
+  const bool sa_ok = a_nscales == M * kbn;
+  const bool sb_ok = b_nscales == kbn * N;
+  char* ws = static_cast<char*>(workspace);
+  size_t left = workspace ? workspace_bytes : 0;
+  float* C = c_f32;
+  if (C == nullptr) {
+    const size_t need = align_up((size_t)M * N * sizeof(float));
+    if (left < need) return MXB_E_WORKSPACE;
+    C = reinterpret_cast<float*>(ws);
+    ws += need;
+    left -= need;
+  }
+  int rc;
+  if (tc_qgemm_eligible(M, K, N, bits, block, sa_ok, sb_ok, a_packed, b_packed, C)) {
+    const size_t need = align_up(tc_qgemm_workspace(M, K, N, bits));
+    if (left < need) return MXB_E_WORKSPACE;
+    rc = tc_qgemm(a_packed, a_scales, b_packed, b_scales, M, K, N, bits, block, C, ws, need, st);
+    ws += need;
+    left -= need;
+  } else {
+    rc = qgemm_generic(a_packed, a_scales, sa_ok, b_packed, b_scales, sb_ok, M, K, N, bits,
+                       block, C, st);
+  }
+  if (rc != MXB_OK || out_bits == 32) return rc;
+  return mxb_requant_f32(C, M * N, block, out_bits, c_packed, c_scales, left ? ws : nullptr,
+                         left, st);
+}
+
+size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int kind,
+                                       int block, int mode) {
+  (void)mode;
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  GemvPlan p = gemv_plan(M, K, N, bits, kind, block, nullptr, nullptr);
+  return p.ok ? p.ws_bytes : 0;
+}
+
+int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const void* w_packed,
+                     const float* w_scales, int64_t N, int bits, int kind, int block, int mode,
+                     float* y, void* workspace, size_t workspace_bytes, void* stream) {
+  if (kind == MXB_KIND_FLOAT ? bits != 4 : !int_bits(bits)) return MXB_E_DTYPE;
+  if (kind != MXB_KIND_INT && kind != MXB_KIND_FLOAT) return MXB_E_DTYPE;
+  if (x_dtype != MXB_F32 && x_dtype != MXB_BF16) return MXB_E_DTYPE;
+  if (mode != MXB_MODE_PARITY && mode != MXB_MODE_FAST) return MXB_E_ARG;
+  if (M < 0 || K <= 0 || N <= 0 || block <= 0) return MXB_E_SHAPE;
+  if (M == 0) return MXB_OK;
+  if (M * K >= (int64_t)1 << 31 || K * N >= (int64_t)1 << 31 || M * N >= (int64_t)1 << 31)
+    return MXB_E_SHAPE;
+  if (!x || !w_packed || !w_scales || !y) return MXB_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GemvPlan p = gemv_plan(M, K, N, bits, kind, block, w_packed, y);
+  if (p.ok) {
+    if (!workspace || workspace_bytes < p.ws_bytes) return MXB_E_WORKSPACE;
+    return gemv_run(p, x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y,
+                    static_cast<float*>(workspace), st);
+  }
+  return wonly_generic(x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y, st);
+}
+
+}  // extern "C"

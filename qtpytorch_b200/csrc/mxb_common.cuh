@@ -1,0 +1,95 @@
+// Shared definitions for the mxb CUDA library (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/mxb.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "mxb is built for sm_100a only"
+#endif
+
+#define MXB_CUDA_TRY(expr)                                 \
+  do {                                                     \
+    cudaError_t _e = (expr);                               \
+    if (_e != cudaSuccess) { mxb_set_cuda_error(_e); return MXB_E_CUDA; } \
+  } while (0)
+
+#define MXB_LAUNCH_CHECK()                                 \
+  do {                                                     \
+    mxb_count_launch();                                    \
+    cudaError_t _e = cudaGetLastError();                   \
+    if (_e != cudaSuccess) { mxb_set_cuda_error(_e); return MXB_E_CUDA; } \
+  } while (0)
+
+void mxb_set_cuda_error(cudaError_t e);
+void mxb_count_launch();
+
+namespace mxb {
+
+constexpr int kSMs = 148;
+
+__host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// NaN-propagating max of |v| (torch.amax propagates NaN).
+__device__ __forceinline__ float amax_step(float acc, float v) {
+  float a = fabsf(v);
+  return (a > acc || a != a) ? a : acc;
+}
+__device__ __forceinline__ float nan_max(float a, float b) {
+  return (a > b || a != a) ? a : b;
+}
+
+// Sorted float4 grid (16 entries, -0 before +0) and its 15 bucket
+// boundaries fl((g[i]+g[i+1])*0.5), as bit patterns.  Values are the
+// normalised E2M1 magnitudes {0,.5,1,1.5,2,3,4,6}/6 and their negatives.
+__device__ __constant__ static const uint32_t kF4Grid[16] = {
+    0xbf800000u, 0xbf2aaaabu, 0xbf000000u, 0xbeaaaaabu, 0xbe800000u, 0xbe2aaaabu,
+    0xbdaaaaabu, 0x80000000u, 0x00000000u, 0x3daaaaabu, 0x3e2aaaabu, 0x3e800000u,
+    0x3eaaaaabu, 0x3f000000u, 0x3f2aaaabu, 0x3f800000u};
+
+__device__ __forceinline__ float f4_grid(int idx) { return __uint_as_float(kF4Grid[idx & 15]); }
+
+// bucketize(v, mids, right=False) == number of boundaries strictly below v.
+__device__ __forceinline__ int f4_bucket(float v) {
+  // boundaries: -5/6, -7/12, -5/12, -7/24, -5/24, -1/8, -1/24, 0, 1/24, 1/8,
+  // 5/24, 7/24, 5/12, 7/12, 5/6 (each the fp32 midpoint of adjacent grid values)
+  const float m0 = __uint_as_float(0xbf555556u), m1 = __uint_as_float(0xbf155556u),
+              m2 = __uint_as_float(0xbed55556u), m3 = __uint_as_float(0xbe955556u),
+              m4 = __uint_as_float(0xbe555556u), m5 = -0.125f,
+              m6 = __uint_as_float(0xbd2aaaabu), m7 = 0.0f,
+              m8 = __uint_as_float(0x3d2aaaabu), m9 = 0.125f,
+              m10 = __uint_as_float(0x3e555556u), m11 = __uint_as_float(0x3e955556u),
+              m12 = __uint_as_float(0x3ed55556u), m13 = __uint_as_float(0x3f155556u),
+              m14 = __uint_as_float(0x3f555556u);
+  int i = (v > m0) + (v > m1) + (v > m2) + (v > m3) + (v > m4) + (v > m5) + (v > m6) +
+          (v > m7) + (v > m8) + (v > m9) + (v > m10) + (v > m11) + (v > m12) +
+          (v > m13) + (v > m14);
+  return i;
+}
+
+// Sign-extend the low `bits` bits of v.
+__device__ __forceinline__ int sext(uint32_t v, int bits) {
+  return (int)(v << (32 - bits)) >> (32 - bits);
+}
+
+// Dequantized value of one code (mxtorch.py:1530-1576 per element).
+template <int BITS, int KIND>
+__device__ __forceinline__ float dequant_code(uint32_t raw, float scale) {
+  if (KIND == MXB_KIND_FLOAT) {
+    return __fmul_rn(f4_grid((int)(raw & 15u)), scale);
+  } else if (BITS == 1) {
+    return (raw & 1u) ? -scale : scale;
+  } else {
+    return __fmul_rn((float)sext(raw, BITS), scale);
+  }
+}
+
+__device__ __forceinline__ float load_as_f32(const float* p, int64_t i) { return __ldg(p + i); }
+__device__ __forceinline__ float load_as_f32(const __nv_bfloat16* p, int64_t i) {
+  return __bfloat162float(p[i]);
+}
+
+}  // namespace mxb

@@ -1,0 +1,44 @@
+// Internal entry points shared between the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+// quantize.cu
+int mxb_requant_f32(const float* c, int64_t n, int block, int out_bits, void* packed,
+                    float* scales, void* ws, size_t wsb, cudaStream_t st);
+size_t mxb_requant_workspace_size(int64_t n, int block);
+
+namespace mxb {
+
+// gemm_cuda_core.cu
+int qgemm_generic(const void* a, const float* sa, bool sa_ok, const void* b, const float* sb,
+                  bool sb_ok, int64_t M, int64_t K, int64_t N, int bits, int block, float* C,
+                  cudaStream_t st);
+int wonly_generic(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
+                  const float* ws, int64_t N, int bits, int kind, int block, float* y,
+                  cudaStream_t st);
+
+// gemv.cu
+struct GemvPlan {
+  bool ok;          // shape/alignment supported by the split-K kernel
+  int splits;       // K splits
+  int krows;        // rows of K per split
+  size_t ws_bytes;  // partial-sum workspace
+};
+GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,
+                   const void* w, const void* y);
+int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_t K,
+             const void* w, const float* ws, int64_t N, int bits, int kind, int block,
+             float* y, float* partial, cudaStream_t st);
+
+// gemm_tc.cu (tcgen05)
+bool tc_qgemm_eligible(int64_t M, int64_t K, int64_t N, int bits, int block, bool sa_ok,
+                       bool sb_ok, const void* a, const void* b, const float* c);
+size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits);
+int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
+             int64_t K, int64_t N, int bits, int block, float* C, void* ws, size_t wsb,
+             cudaStream_t st);
+
+}  // namespace mxb

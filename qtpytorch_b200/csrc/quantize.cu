@@ -1,0 +1,681 @@
+// Quantize / pack, dequantize and the randomized Hadamard transform.
+//
+// All three are HBM-bound byte work.  The vectorised kernels give each
+// thread 8 consecutive elements (two 16-byte loads of fp32, one of bf16);
+// `block / 8` adjacent lanes own one scale block and reduce its absmax with
+// warp shuffles, then each thread writes its 8 packed codes with one store.
+// Generic kernels cover the remaining shapes (odd block sizes, unaligned
+// pointers).  Rounding follows the reference's fp32 operation order exactly
+// (mxtorch.py:1426-1528): reciprocal-then-multiply for the integer scale,
+// true division for float4 and for the matmul requantization, round half to
+// even.  Built without fast-math so every `__f*_rn` is one IEEE rounding.
+#include "mxb_common.cuh"
+
+#include <math.h>
+#include <string.h>
+
+#include <atomic>
+
+using namespace mxb;
+
+namespace {
+
+// Quantizer flavours.
+enum QMode { Q_INT_RECIP = 0, Q_INT_DIV = 1, Q_FLOAT4 = 2 };
+
+__device__ __forceinline__ float clamp_keep_nan(float v, float m) {
+  return v < -m ? -m : (v > m ? m : v);
+}
+
+// Per-block factor: returns scale (stored) and `mul` (what codes use).
+template <int BITS, int MODE>
+__device__ __forceinline__ void block_factor(float amax, float& scale, float& mul) {
+  float a = amax < 1e-12f ? 1e-12f : amax;  // clamp(min=1e-12), NaN kept
+  if (MODE == Q_FLOAT4 || (MODE == Q_INT_RECIP && BITS == 1)) {
+    scale = a;
+    mul = a;
+  } else if (MODE == Q_INT_RECIP) {
+    const float max_int = (float)((1 << (BITS - 1)) - 1);
+    float si = __fmul_rn(__frcp_rn(a), max_int);  // max_int / a  (torch __rdiv__)
+    scale = __frcp_rn(si);                        // scale_inv.reciprocal()
+    mul = si;
+  } else {  // Q_INT_DIV: requantization of the matmul output
+    const float max_out = (float)((1 << (BITS - 1)) - 1);
+    scale = __fdiv_rn(a, max_out);
+    mul = scale;
+  }
+}
+
+template <int BITS, int MODE>
+__device__ __forceinline__ uint32_t code_of(float v, float mul) {
+  if (MODE == Q_FLOAT4) {
+    return (uint32_t)f4_bucket(__fdiv_rn(v, mul));
+  } else if (MODE == Q_INT_RECIP && BITS == 1) {
+    return (v >= 0.0f) ? 0u : 1u;  // where(x >= 0, 0, -1); NaN -> -1
+  } else {
+    const float m = (float)((1 << (BITS - 1)) - 1);
+    float q = (MODE == Q_INT_RECIP) ? __fmul_rn(v, mul) : __fdiv_rn(v, mul);
+    q = clamp_keep_nan(q, m);
+    int c = __float2int_rn(q);  // round half to even; NaN -> 0 after masking
+    return (uint32_t)c & ((1u << BITS) - 1u);
+  }
+}
+
+// Quantize 8 consecutive values owned by this lane; `L` lanes form a block.
+// Writes the packed codes of these 8 elements at byte offset (e0 * BITS / 8).
+template <int BITS, int MODE>
+__device__ __forceinline__ void quant8_store(const float (&v)[8], bool valid, int L,
+                                             int64_t e0, uint8_t* __restrict__ packed,
+                                             float* __restrict__ scales, int64_t blk) {
+  float a = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a = amax_step(a, v[i]);
+  for (int o = L >> 1; o > 0; o >>= 1) a = nan_max(a, __shfl_xor_sync(0xffffffffu, a, o));
+  if (!valid) return;
+  float scale, mul;
+  block_factor<BITS, MODE>(a, scale, mul);
+  if ((threadIdx.x & (L - 1)) == 0) scales[blk] = scale;
+  uint32_t c[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = code_of<BITS, MODE>(v[i], mul);
+  uint8_t* p = packed + (e0 * BITS) / 8;
+  if (BITS == 8) {
+    uint2 w;
+    w.x = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
+    w.y = c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24);
+    *reinterpret_cast<uint2*>(p) = w;
+  } else if (BITS == 16) {
+    uint4 w;
+    w.x = c[0] | (c[1] << 16);
+    w.y = c[2] | (c[3] << 16);
+    w.z = c[4] | (c[5] << 16);
+    w.w = c[6] | (c[7] << 16);
+    *reinterpret_cast<uint4*>(p) = w;
+  } else if (BITS == 4) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= c[i] << (4 * i);
+    *reinterpret_cast<uint32_t*>(p) = w;
+  } else if (BITS == 2) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= c[i] << (2 * i);
+    *reinterpret_cast<uint16_t*>(p) = (uint16_t)w;
+  } else {  // BITS == 1
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= c[i] << i;
+    *p = (uint8_t)w;
+  }
+}
+
+template <typename InT>
+__device__ __forceinline__ void load8(const InT* __restrict__ x, int64_t e0, int64_t n,
+                                      bool vec, float (&v)[8]) {
+  if (vec && e0 + 8 <= n) {
+    if (sizeof(InT) == 4) {
+      const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + e0);
+      float4 a = __ldcs(p), b = __ldcs(p + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+      uint4 r = __ldcs(reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(x) + e0));
+      uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (e0 + i < n) ? load_as_f32(x, e0 + i) : 0.0f;
+  }
+}
+
+// Vectorised quantize: block in {8,16,32,64,128,256}.
+template <typename InT, int BITS, int MODE>
+__global__ void __launch_bounds__(256) quant_vec_kernel(const InT* __restrict__ x, int64_t n,
+                                                        int block, int64_t nb, bool vec,
+                                                        uint8_t* __restrict__ packed,
+                                                        float* __restrict__ scales) {
+  const int L = block / 8;
+  const int64_t groups = nb * (int64_t)L;  // threads with work
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t w = warp0; w * 32 < groups; w += nwarps) {
+    const int64_t t = w * 32 + lane;
+    const bool valid = t < groups;
+    float v[8];
+    load8<InT>(x, t * 8, valid ? n : 0, vec, v);
+    quant8_store<BITS, MODE>(v, valid, L, t * 8, packed, scales, t / L);
+  }
+}
+
+// Generic pass 1: one warp per block -> scale and code multiplier.
+template <typename InT, int BITS, int MODE>
+__global__ void __launch_bounds__(256) quant_scales_kernel(const InT* __restrict__ x, int64_t n,
+                                                           int block, int64_t nb,
+                                                           float* __restrict__ scales,
+                                                           float* __restrict__ muls) {
+  const int lane = threadIdx.x & 31;
+  int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (; b < nb; b += nw) {
+    float a = 0.0f;
+    const int64_t e0 = b * block;
+    for (int i = lane; i < block; i += 32) {
+      int64_t e = e0 + i;
+      if (e < n) a = amax_step(a, load_as_f32(x, e));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = nan_max(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (lane == 0) {
+      float s, m;
+      block_factor<BITS, MODE>(a, s, m);
+      scales[b] = s;
+      muls[b] = m;
+    }
+  }
+}
+
+// Generic pass 2: one thread per packed storage word (8 bits, or 32 for 16-bit codes).
+template <typename InT, int BITS, int MODE>
+__global__ void __launch_bounds__(256) quant_pack_kernel(const InT* __restrict__ x, int64_t n,
+                                                         int block, int64_t ncodes,
+                                                         int64_t nwords,
+                                                         const float* __restrict__ muls,
+                                                         uint8_t* __restrict__ packed) {
+  constexpr int WBITS = BITS == 16 ? 32 : 8;
+  constexpr int PER = WBITS / BITS;
+  for (int64_t wi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; wi < nwords;
+       wi += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      int64_t e = wi * PER + i;
+      if (e >= ncodes) break;  // storage padding beyond the last block: code 0
+      float v = e < n ? load_as_f32(x, e) : 0.0f;
+      word |= code_of<BITS, MODE>(v, muls[e / block]) << (i * BITS);
+    }
+    if (BITS == 16)
+      reinterpret_cast<uint32_t*>(packed)[wi] = word;
+    else
+      packed[wi] = (uint8_t)word;
+  }
+}
+
+// ── dequantize ───────────────────────────────────────────────────────────────
+template <int BITS>
+__device__ __forceinline__ uint32_t raw_code(const uint8_t* __restrict__ packed, int64_t e) {
+  if constexpr (BITS == 16) {
+    uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(packed) + (e >> 1));
+    return (w >> ((e & 1) * 16)) & 0xffffu;
+  }
+  constexpr int PER = BITS >= 8 ? 1 : 8 / BITS;
+  uint32_t b = __ldg(packed + e / PER);
+  return (b >> ((e % PER) * BITS)) & ((1u << BITS) - 1u);
+}
+
+template <int BITS, int KIND>
+__global__ void __launch_bounds__(256) dequant_vec_kernel(const uint8_t* __restrict__ packed,
+                                                          const float* __restrict__ scales,
+                                                          int64_t n, int block,
+                                                          float* __restrict__ out) {
+  const int64_t ngroups = (n + 7) / 8;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ngroups;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = t * 8;
+    const float s = __ldg(scales + e0 / block);
+    uint32_t c[8];
+    const uint8_t* p = packed + (e0 * BITS) / 8;
+    if (BITS == 8) {
+      uint2 w = __ldcs(reinterpret_cast<const uint2*>(p));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { c[i] = (w.x >> (8 * i)) & 0xff; c[i + 4] = (w.y >> (8 * i)) & 0xff; }
+    } else if (BITS == 16) {
+      uint4 w = __ldcs(reinterpret_cast<const uint4*>(p));
+      uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { c[2 * i] = ws[i] & 0xffff; c[2 * i + 1] = ws[i] >> 16; }
+    } else {
+      uint32_t w;
+      if (BITS == 4) w = __ldcs(reinterpret_cast<const uint32_t*>(p));
+      else if (BITS == 2) w = __ldcs(reinterpret_cast<const uint16_t*>(p));
+      else w = *p;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) c[i] = (w >> (BITS * i)) & ((1u << BITS) - 1u);
+    }
+    float r[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = dequant_code<BITS, KIND>(c[i], s);
+    if (e0 + 8 <= n) {
+      float4* o = reinterpret_cast<float4*>(out + e0);
+      __stcs(o, make_float4(r[0], r[1], r[2], r[3]));
+      __stcs(o + 1, make_float4(r[4], r[5], r[6], r[7]));
+    } else {
+      for (int i = 0; i < 8; ++i)
+        if (e0 + i < n) out[e0 + i] = r[i];
+    }
+  }
+}
+
+template <int BITS, int KIND>
+__global__ void __launch_bounds__(256) dequant_generic_kernel(const uint8_t* __restrict__ packed,
+                                                              const float* __restrict__ scales,
+                                                              int64_t n, int block,
+                                                              float* __restrict__ out) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x)
+    out[e] = dequant_code<BITS, KIND>(raw_code<BITS>(packed, e), __ldg(scales + e / block));
+}
+
+// ── Walsh–Hadamard transform of one row held in shared memory ────────────────
+// Stage order is the reference's (mxtorch.py:2811-2832): stride n/2 first,
+// down to 1, each pair (e, o) -> (e + o, e - o).  Strides >= 32 run as
+// radix-2^R passes in registers; strides < 32 with warp shuffles.
+template <int R>
+__device__ __forceinline__ void wht_pass(float* s, int n, int lo) {
+  constexpr int RR = 1 << R;
+  const int nbase = n >> R;
+  const int hi = lo + R;
+  for (int b = threadIdx.x; b < nbase; b += blockDim.x) {
+    const int base = (b & ((1 << lo) - 1)) | ((b >> lo) << hi);
+    float v[RR];
+#pragma unroll
+    for (int j = 0; j < RR; ++j) v[j] = s[base + (j << lo)];
+#pragma unroll
+    for (int q = R - 1; q >= 0; --q) {
+#pragma unroll
+      for (int j = 0; j < RR; ++j) {
+        if (!(j & (1 << q))) {
+          float e = v[j], o = v[j + (1 << q)];
+          v[j] = __fadd_rn(e, o);
+          v[j + (1 << q)] = __fsub_rn(e, o);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < RR; ++j) s[base + (j << lo)] = v[j];
+  }
+}
+
+// In-warp stages for strides min(n,32)/2 .. 1 on value v at index i (lane = i & 31).
+__device__ __forceinline__ float wht_low(float v, int n) {
+  const int lane = threadIdx.x & 31;
+  const int top = n < 32 ? n : 32;
+  for (int h = top >> 1; h > 0; h >>= 1) {
+    float p = __shfl_xor_sync(0xffffffffu, v, h);
+    v = (lane & h) ? __fsub_rn(p, v) : __fadd_rn(v, p);
+  }
+  return v;
+}
+
+// Full transform (without the 1/sqrt(n)); leaves the result in s.
+__device__ void wht_row(float* s, int n) {
+  int L = 31 - __clz(n);
+  int hi = L;
+  while (hi > 5) {
+    int r = hi - 5 < 4 ? hi - 5 : 4;
+    int lo = hi - r;
+    __syncthreads();
+    switch (r) {
+      case 4: wht_pass<4>(s, n, lo); break;
+      case 3: wht_pass<3>(s, n, lo); break;
+      case 2: wht_pass<2>(s, n, lo); break;
+      default: wht_pass<1>(s, n, lo); break;
+    }
+    hi = lo;
+  }
+  __syncthreads();
+  const int span = n < 32 ? 32 : n;
+  for (int i0 = threadIdx.x & ~31; i0 < span; i0 += blockDim.x) {
+    int i = i0 + (threadIdx.x & 31);
+    float v = (i < n) ? s[i] : 0.0f;
+    v = wht_low(v, n);
+    if (i < n) s[i] = v;
+  }
+  __syncthreads();
+}
+
+// Load one row: s[i] = x[i] * sign[i] (rotate) or x[i] (unrotate) for i < d, 0 above.
+template <typename InT>
+__device__ __forceinline__ void load_row(float* s, const InT* __restrict__ xr, int d, int n,
+                                         const float* __restrict__ signs, bool mul_signs) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = 0.0f;
+    if (i < d) {
+      v = load_as_f32(xr, i);
+      if (mul_signs) v = __fmul_rn(v, __ldg(signs + i));
+    }
+    s[i] = v;
+  }
+}
+
+// Rotate each row, then (fuse_quant) quantize it in place, or write the
+// rotated fp32 row to `rot_out`.
+template <typename InT, int BITS, int MODE>
+__global__ void __launch_bounds__(256) hquant_kernel(const InT* __restrict__ x, int d, int n,
+                                                     float sqrtn, const float* __restrict__ signs,
+                                                     int block, bool fuse_quant,
+                                                     uint8_t* __restrict__ packed,
+                                                     float* __restrict__ scales,
+                                                     float* __restrict__ rot_out) {
+  extern __shared__ __align__(16) float srow[];
+  const int64_t r = blockIdx.x;
+  load_row<InT>(srow, x + r * d, d, n, signs, true);
+  wht_row(srow, n);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) srow[i] = __fdiv_rn(srow[i], sqrtn);
+  __syncthreads();
+  if (!fuse_quant) {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) rot_out[r * d + i] = srow[i];
+    return;
+  }
+  // d % block == 0 and block in {8..256}: blocks are row-local.
+  const int L = block / 8;
+  const int groups = d / 8;
+  const int lane = threadIdx.x & 31;
+  const int64_t row_e0 = r * (int64_t)d;
+  const int64_t row_b0 = row_e0 / block;
+  for (int w = (threadIdx.x >> 5) * 32; w < groups; w += blockDim.x) {
+    const int t = w + lane;
+    const bool valid = t < groups;
+    float v[8];
+    if (valid) {
+      float4 a = *reinterpret_cast<const float4*>(srow + 8 * t);
+      float4 b = *reinterpret_cast<const float4*>(srow + 8 * t + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    quant8_store<BITS, MODE>(v, valid, L, row_e0 + 8 * t, packed, scales, row_b0 + t / L);
+  }
+}
+
+// Dequantize each row's codes, then unrotate.
+template <int BITS, int KIND>
+__global__ void __launch_bounds__(256) hdequant_kernel(const uint8_t* __restrict__ packed,
+                                                       const float* __restrict__ scales,
+                                                       int d, int n, float sqrtn,
+                                                       const float* __restrict__ signs,
+                                                       int block, float* __restrict__ out) {
+  extern __shared__ __align__(16) float srow[];
+  const int64_t r = blockIdx.x;
+  const int64_t e0 = r * (int64_t)d;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = 0.0f;
+    if (i < d) {
+      int64_t e = e0 + i;
+      v = dequant_code<BITS, KIND>(raw_code<BITS>(packed, e), __ldg(scales + e / block));
+    }
+    srow[i] = v;
+  }
+  wht_row(srow, n);
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    out[e0 + i] = __fmul_rn(__fdiv_rn(srow[i], sqrtn), __ldg(signs + i));
+}
+
+__global__ void __launch_bounds__(256) hrows_kernel(const float* __restrict__ x, int d, int n,
+                                                    float sqrtn, const float* __restrict__ signs,
+                                                    bool inverse, float* __restrict__ out) {
+  extern __shared__ __align__(16) float srow[];
+  const int64_t r = blockIdx.x;
+  load_row<float>(srow, x + r * d, d, n, signs, !inverse);
+  wht_row(srow, n);  // begins and ends with __syncthreads, so in-place is safe
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float v = __fdiv_rn(srow[i], sqrtn);
+    if (inverse) v = __fmul_rn(v, __ldg(signs + i));
+    out[r * d + i] = v;
+  }
+}
+
+// ── host side ────────────────────────────────────────────────────────────────
+constexpr int kMaxHadamardN = 32768;
+
+bool pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
+int64_t pow2ceil(int64_t d) {
+  int64_t n = 1;
+  while (n < d) n <<= 1;
+  return n;
+}
+bool vec_block(int block) { return block >= 8 && block <= 256 && pow2(block); }
+
+int grid_for(int64_t work_threads, int threads = 256) {
+  int64_t g = cdiv(work_threads, threads);
+  int64_t cap = (int64_t)kSMs * 16;
+  if (g > cap) g = cap;
+  return (int)(g < 1 ? 1 : g);
+}
+
+bool valid_dtype(int bits, int kind) {
+  if (kind == MXB_KIND_FLOAT) return bits == 4;
+  if (kind == MXB_KIND_INT) return bits == 1 || bits == 2 || bits == 4 || bits == 8;
+  return false;
+}
+
+bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+// Launch the base quantizer on a flat input.
+template <typename InT, int BITS, int MODE>
+int quant_flat(const InT* x, int64_t n, int block, uint8_t* packed, float* scales,
+               void* ws, size_t ws_bytes, cudaStream_t st) {
+  const int64_t nb = cdiv(n, block);
+  const size_t store_align = BITS == 16 ? 16 : (BITS == 8 ? 8 : BITS / 1);
+  const bool out_ok = aligned(packed, store_align < 1 ? 1 : store_align);
+  if (vec_block(block) && out_ok) {
+    const bool vec = aligned(x, 16);
+    quant_vec_kernel<InT, BITS, MODE><<<grid_for(nb * (block / 8)), 256, 0, st>>>(
+        x, n, block, nb, vec, packed, scales);
+    MXB_LAUNCH_CHECK();
+    return MXB_OK;
+  }
+  if (BITS == 16 && !aligned(packed, 4)) return MXB_E_ALIGN;
+  if (ws == nullptr || ws_bytes < (size_t)nb * sizeof(float)) return MXB_E_WORKSPACE;
+  float* muls = static_cast<float*>(ws);
+  quant_scales_kernel<InT, BITS, MODE><<<grid_for(nb * 32), 256, 0, st>>>(x, n, block, nb,
+                                                                          scales, muls);
+  MXB_LAUNCH_CHECK();
+  const int per = BITS == 16 ? 2 : 8 / BITS;
+  const int64_t ncodes = nb * block;
+  const int64_t nwords = cdiv(ncodes, per);
+  quant_pack_kernel<InT, BITS, MODE><<<grid_for(nwords), 256, 0, st>>>(x, n, block, ncodes,
+                                                                      nwords, muls, packed);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+template <typename InT, int BITS, int MODE>
+int quant_dispatch(const InT* x, int64_t n, int64_t row_len, int variant, int block,
+                   const float* signs, uint8_t* packed, float* scales, void* ws,
+                   size_t ws_bytes, cudaStream_t st) {
+  if (variant == MXB_VAR_BASE)
+    return quant_flat<InT, BITS, MODE>(x, n, block, packed, scales, ws, ws_bytes, st);
+  // Hadamard variant
+  const int64_t d = row_len;
+  const int64_t hn = pow2ceil(d);
+  if (d <= 0 || n % d != 0 || hn > kMaxHadamardN) return MXB_E_SHAPE;
+  if (signs == nullptr) return MXB_E_ARG;
+  const int64_t rows = n / d;
+  const float sqrtn = (float)sqrt((double)hn);
+  const size_t smem = (size_t)hn * sizeof(float);
+  auto kern = hquant_kernel<InT, BITS, MODE>;
+  MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kMaxHadamardN * (int)sizeof(float)));
+  const bool fuse = vec_block(block) && d % block == 0 && aligned(packed, 8);
+  if (fuse) {
+    kern<<<(unsigned)rows, 256, smem, st>>>(x, (int)d, (int)hn, sqrtn, signs, block, true,
+                                            packed, scales, nullptr);
+    MXB_LAUNCH_CHECK();
+    return MXB_OK;
+  }
+  const size_t rot_bytes = ((size_t)n * sizeof(float) + 255) & ~(size_t)255;
+  if (ws == nullptr || ws_bytes < rot_bytes) return MXB_E_WORKSPACE;
+  float* rot = static_cast<float*>(ws);
+  kern<<<(unsigned)rows, 256, smem, st>>>(x, (int)d, (int)hn, sqrtn, signs, block, false,
+                                          packed, scales, rot);
+  MXB_LAUNCH_CHECK();
+  return quant_flat<float, BITS, MODE>(rot, n, block, packed, scales,
+                                       static_cast<char*>(ws) + rot_bytes,
+                                       ws_bytes - rot_bytes, st);
+}
+
+template <typename InT>
+int quant_by_dtype(const InT* x, int64_t n, int64_t row_len, int bits, int kind, int variant,
+                   int block, const float* signs, uint8_t* packed, float* scales, void* ws,
+                   size_t wsb, cudaStream_t st) {
+  if (kind == MXB_KIND_FLOAT)
+    return quant_dispatch<InT, 4, Q_FLOAT4>(x, n, row_len, variant, block, signs, packed,
+                                            scales, ws, wsb, st);
+  switch (bits) {
+    case 1: return quant_dispatch<InT, 1, Q_INT_RECIP>(x, n, row_len, variant, block, signs, packed, scales, ws, wsb, st);
+    case 2: return quant_dispatch<InT, 2, Q_INT_RECIP>(x, n, row_len, variant, block, signs, packed, scales, ws, wsb, st);
+    case 4: return quant_dispatch<InT, 4, Q_INT_RECIP>(x, n, row_len, variant, block, signs, packed, scales, ws, wsb, st);
+    case 8: return quant_dispatch<InT, 8, Q_INT_RECIP>(x, n, row_len, variant, block, signs, packed, scales, ws, wsb, st);
+  }
+  return MXB_E_DTYPE;
+}
+
+template <int BITS, int KIND>
+int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_t row_len,
+                   int variant, int block, const float* signs, float* out, cudaStream_t st) {
+  if (variant == MXB_VAR_H) {
+    const int64_t d = row_len;
+    const int64_t hn = pow2ceil(d);
+    if (d <= 0 || n % d != 0 || hn > kMaxHadamardN) return MXB_E_SHAPE;
+    if (signs == nullptr) return MXB_E_ARG;
+    auto kern = hdequant_kernel<BITS, KIND>;
+    MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kMaxHadamardN * (int)sizeof(float)));
+    kern<<<(unsigned)(n / d), 256, hn * sizeof(float), st>>>(
+        packed, scales, (int)d, (int)hn, (float)sqrt((double)hn), signs, block, out);
+    MXB_LAUNCH_CHECK();
+    return MXB_OK;
+  }
+  const size_t in_align = BITS == 16 ? 16 : (BITS == 8 ? 8 : (BITS == 4 ? 4 : (BITS == 2 ? 2 : 1)));
+  if (block % 8 == 0 && aligned(packed, in_align) && aligned(out, 16)) {
+    dequant_vec_kernel<BITS, KIND><<<grid_for(cdiv(n, 8)), 256, 0, st>>>(packed, scales, n,
+                                                                         block, out);
+  } else {
+    dequant_generic_kernel<BITS, KIND><<<grid_for(n), 256, 0, st>>>(packed, scales, n, block,
+                                                                    out);
+  }
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+}  // namespace
+
+// Used by the matmul's requantization.
+int mxb_requant_f32(const float* c, int64_t n, int block, int out_bits, void* packed,
+                    float* scales, void* ws, size_t wsb, cudaStream_t st) {
+  uint8_t* p = static_cast<uint8_t*>(packed);
+  switch (out_bits) {
+    case 2: return quant_flat<float, 2, Q_INT_DIV>(c, n, block, p, scales, ws, wsb, st);
+    case 4: return quant_flat<float, 4, Q_INT_DIV>(c, n, block, p, scales, ws, wsb, st);
+    case 8: return quant_flat<float, 8, Q_INT_DIV>(c, n, block, p, scales, ws, wsb, st);
+    case 16: return quant_flat<float, 16, Q_INT_DIV>(c, n, block, p, scales, ws, wsb, st);
+  }
+  return MXB_E_DTYPE;
+}
+
+size_t mxb_requant_workspace_size(int64_t n, int block) {
+  return vec_block(block) ? 0 : (size_t)cdiv(n, block) * sizeof(float);
+}
+
+static thread_local char g_last_error[256] = "";
+static std::atomic<unsigned long long> g_launches{0};
+
+void mxb_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void mxb_set_cuda_error(cudaError_t e) {
+  strncpy(g_last_error, cudaGetErrorString(e), sizeof(g_last_error) - 1);
+}
+
+extern "C" {
+
+int mxb_version(void) { return 100; }
+
+const char* mxb_last_error(void) { return g_last_error; }
+
+uint64_t mxb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+size_t mxb_packed_bytes(int64_t n, int bits, int block) {
+  if (n < 0 || block <= 0) return 0;
+  const int64_t codes = cdiv(n, block) * block;
+  if (bits == 16) return (size_t)cdiv(codes, 2) * 4;
+  if (bits != 1 && bits != 2 && bits != 4 && bits != 8) return 0;
+  return (size_t)cdiv(codes * bits, 8);
+}
+
+size_t mxb_quantize_workspace_size(int64_t n, int64_t row_len, int bits, int kind, int variant,
+                                   int block) {
+  (void)bits; (void)kind;
+  if (n <= 0 || block <= 0) return 0;
+  size_t flat = vec_block(block) ? 0 : (size_t)cdiv(n, block) * sizeof(float);
+  if (variant != MXB_VAR_H) return flat;
+  if (vec_block(block) && row_len > 0 && row_len % block == 0) return 0;
+  return (((size_t)n * sizeof(float) + 255) & ~(size_t)255) + flat;
+}
+
+int mxb_quantize(const void* x, int x_dtype, int64_t n, int64_t row_len, int bits, int kind,
+                 int variant, int block, const float* signs, void* packed, float* scales,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (!valid_dtype(bits, kind)) return MXB_E_DTYPE;
+  if (variant != MXB_VAR_BASE && variant != MXB_VAR_H) return MXB_E_DTYPE;
+  if (n < 0 || block <= 0) return MXB_E_SHAPE;
+  if (n == 0) return MXB_OK;
+  if (!x || !packed || !scales) return MXB_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* p = static_cast<uint8_t*>(packed);
+  if (x_dtype == MXB_F32)
+    return quant_by_dtype<float>(static_cast<const float*>(x), n, row_len, bits, kind, variant,
+                                 block, signs, p, scales, workspace, workspace_bytes, st);
+  if (x_dtype == MXB_BF16)
+    return quant_by_dtype<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x), n, row_len,
+                                         bits, kind, variant, block, signs, p, scales,
+                                         workspace, workspace_bytes, st);
+  return MXB_E_DTYPE;
+}
+
+int mxb_dequantize(const void* packed, const float* scales, int64_t n, int64_t row_len,
+                   int bits, int kind, int variant, int block, const float* signs, float* out,
+                   void* stream) {
+  if (!(valid_dtype(bits, kind) || (bits == 16 && kind == MXB_KIND_INT))) return MXB_E_DTYPE;
+  if (variant != MXB_VAR_BASE && variant != MXB_VAR_H) return MXB_E_DTYPE;
+  if (n < 0 || block <= 0) return MXB_E_SHAPE;
+  if (n == 0) return MXB_OK;
+  if (!packed || !scales || !out) return MXB_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* p = static_cast<const uint8_t*>(packed);
+  if (kind == MXB_KIND_FLOAT)
+    return dequant_launch<4, MXB_KIND_FLOAT>(p, scales, n, row_len, variant, block, signs, out, st);
+  switch (bits) {
+    case 1: return dequant_launch<1, MXB_KIND_INT>(p, scales, n, row_len, variant, block, signs, out, st);
+    case 2: return dequant_launch<2, MXB_KIND_INT>(p, scales, n, row_len, variant, block, signs, out, st);
+    case 4: return dequant_launch<4, MXB_KIND_INT>(p, scales, n, row_len, variant, block, signs, out, st);
+    case 8: return dequant_launch<8, MXB_KIND_INT>(p, scales, n, row_len, variant, block, signs, out, st);
+    case 16: return dequant_launch<16, MXB_KIND_INT>(p, scales, n, row_len, variant, block, signs, out, st);
+  }
+  return MXB_E_DTYPE;
+}
+
+int mxb_hadamard_rows(const float* x, int64_t rows, int64_t d, const float* signs, int inverse,
+                      float* out, void* stream) {
+  if (rows < 0 || d <= 0) return MXB_E_SHAPE;
+  if (rows == 0) return MXB_OK;
+  if (!x || !signs || !out) return MXB_E_ARG;
+  const int64_t hn = pow2ceil(d);
+  if (hn > kMaxHadamardN) return MXB_E_SHAPE;
+  MXB_CUDA_TRY(cudaFuncSetAttribute(hrows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kMaxHadamardN * (int)sizeof(float)));
+  hrows_kernel<<<(unsigned)rows, 256, hn * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+      x, (int)d, (int)hn, (float)sqrt((double)hn), signs, inverse != 0, out);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+}  // extern "C"

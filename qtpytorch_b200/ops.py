@@ -1,0 +1,184 @@
+"""Tensor-level wrappers of the mxb C ABI (no autograd, no dispatch).
+
+Each function takes and returns torch tensors on a CUDA device, allocates
+outputs and workspaces with torch, and launches on the current stream.
+CPU inputs are copied to the current CUDA device first; nothing here
+computes on the CPU.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib as L
+from .dtypes import KERNEL_BITS, get_mx_dtype, mx_dtype
+from .hadamard import device_signs
+
+
+def _device_of(x: torch.Tensor) -> torch.device:
+    if x.is_cuda:
+        return x.device
+    if not torch.cuda.is_available():
+        raise L.MxbError("qtpytorch_b200 needs a CUDA device (B200, sm_100a)")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def kernel_dtype_ok(dt: mx_dtype) -> bool:
+    if dt.variant not in ("", "h"):
+        return False
+    if dt.is_float:
+        return dt.bits == 4
+    return dt.bits in KERNEL_BITS
+
+
+def _kind(dt: mx_dtype) -> int:
+    return L.KIND_FLOAT if dt.is_float else L.KIND_INT
+
+
+def _check_dtype(dt: mx_dtype) -> None:
+    if not kernel_dtype_ok(dt):
+        raise NotImplementedError(
+            f"{dt.name}: the B200 kernels cover int1/int2/int4/int8 'd'/'u' and float4, "
+            f"base and 'h' variants")
+
+
+def row_len_of(shape) -> int:
+    n = 1
+    for s in shape:
+        n *= int(s)
+    if len(shape) >= 2:
+        return int(shape[-1])
+    return max(n, 1)
+
+
+def quantize(x: torch.Tensor, dt, block: int = 128) -> Tuple[torch.Tensor, torch.Tensor, int]:
+    """(packed int8, scales fp32 [nb], n): mxtorch ``quantize`` (mxtorch.py:1684-1763)."""
+    dt = get_mx_dtype(dt)
+    _check_dtype(dt)
+    if block <= 0:
+        raise ValueError("block must be positive")
+    dev = _device_of(x)
+    x = x.detach()
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float()
+    x = x.to(dev).contiguous()
+    n = x.numel()
+    nb = -(-n // block)
+    lib = L.load()
+    packed = torch.empty(lib.mxb_packed_bytes(n, dt.bits, block), dtype=torch.int8, device=dev)
+    scales = torch.empty(nb, dtype=torch.float32, device=dev)
+    if n == 0:
+        return packed, scales, 0
+    row_len = row_len_of(x.shape)
+    variant = L.VAR_H if dt.is_hadamard else L.VAR_BASE
+    signs = device_signs(row_len, dt.hadamard_seed, dev) if dt.is_hadamard else None
+    kind = _kind(dt)
+    in_t = L.BF16 if x.dtype == torch.bfloat16 else L.F32
+    wsb = lib.mxb_quantize_workspace_size(n, row_len, dt.bits, kind, variant, block)
+    ws = L.workspace(wsb, dev)
+    with torch.cuda.device(dev):
+        rc = lib.mxb_quantize(L.ptr(x), in_t, n, row_len, dt.bits, kind, variant, block,
+                              L.ptr(signs), L.ptr(packed), L.ptr(scales), L.ptr(ws), wsb,
+                              L.stream_of(dev))
+    L.check(rc, f"mxb_quantize({dt.name}, n={n}, block={block})")
+    return packed, scales, n
+
+
+def dequantize(packed: torch.Tensor, scales: torch.Tensor, dt, n: int, block: int,
+               shape=None) -> torch.Tensor:
+    """fp32 tensor of ``shape`` (flat if None): mxtorch ``_dequant`` (mxtorch.py:1530-1597).
+
+    For ``h`` dtypes the inverse rotation runs along the last dim of ``shape``.
+    """
+    dt = get_mx_dtype(dt)
+    if not (kernel_dtype_ok(dt) or (dt.is_int and dt.bits == 16 and dt.variant == "")):
+        raise NotImplementedError(f"dequantize of {dt.name} is not on the B200 path")
+    L.require_cuda(packed, "dequantize")
+    dev = packed.device
+    shape = tuple(shape) if shape is not None else (n,)
+    out = torch.empty(n, dtype=torch.float32, device=dev)
+    if n == 0:
+        return out.reshape(shape)
+    row_len = row_len_of(shape)
+    variant = L.VAR_H if dt.is_hadamard else L.VAR_BASE
+    signs = device_signs(row_len, dt.hadamard_seed, dev) if dt.is_hadamard else None
+    lib = L.load()
+    with torch.cuda.device(dev):
+        rc = lib.mxb_dequantize(L.ptr(packed.contiguous()), L.ptr(scales.contiguous()), n,
+                                row_len, dt.bits, _kind(dt), variant, block, L.ptr(signs),
+                                L.ptr(out), L.stream_of(dev))
+    L.check(rc, f"mxb_dequantize({dt.name}, n={n})")
+    return out.reshape(shape)
+
+
+def hadamard_rows(y: torch.Tensor, seed: int, inverse: bool) -> torch.Tensor:
+    """Randomized WHT along the last dim of a fp32 CUDA tensor (in a new tensor)."""
+    L.require_cuda(y, "hadamard_rows")
+    y = y.float().contiguous()
+    d = y.shape[-1]
+    rows = y.numel() // max(d, 1)
+    out = torch.empty_like(y)
+    signs = device_signs(d, seed, y.device)
+    with torch.cuda.device(y.device):
+        rc = L.load().mxb_hadamard_rows(L.ptr(y), rows, d, L.ptr(signs), int(inverse),
+                                        L.ptr(out), L.stream_of(y.device))
+    L.check(rc, "mxb_hadamard_rows")
+    return out
+
+
+def qgemm(a_packed, a_scales, b_packed, b_scales, M: int, K: int, N: int, bits: int,
+          block: int, out_bits: int, want_f32: bool = False):
+    """Packed integer matmul (mxtorch.py:5497-5573 CPU branch, bit-exact).
+
+    Returns (c_packed, c_scales, c_f32 or None); c_packed is int32 words for
+    16-bit codes, int8 bytes otherwise.
+    """
+    L.require_cuda(a_packed, "qgemm")
+    dev = a_packed.device
+    lib = L.load()
+    nb = -(-(M * N) // block)
+    nbytes = lib.mxb_packed_bytes(M * N, out_bits, block)
+    if out_bits == 16:
+        c_packed = torch.empty(nbytes // 4, dtype=torch.int32, device=dev)
+    else:
+        c_packed = torch.empty(nbytes, dtype=torch.int8, device=dev)
+    c_scales = torch.empty(nb, dtype=torch.float32, device=dev)
+    c_f32 = torch.empty(M, N, dtype=torch.float32, device=dev) if want_f32 else None
+    wsb = lib.mxb_qgemm_workspace_size(M, K, N, bits, block)
+    ws = L.workspace(wsb, dev)
+    a_packed, b_packed = a_packed.contiguous(), b_packed.to(dev).contiguous()
+    a_scales, b_scales = a_scales.contiguous(), b_scales.to(dev).contiguous()
+    with torch.cuda.device(dev):
+        rc = lib.mxb_qgemm(L.ptr(a_packed), L.ptr(a_scales), a_scales.numel(),
+                           L.ptr(b_packed), L.ptr(b_scales), b_scales.numel(), M, K, N, bits,
+                           block, out_bits, L.ptr(c_packed), L.ptr(c_scales), L.ptr(c_f32),
+                           L.ptr(ws), wsb, L.stream_of(dev))
+    L.check(rc, f"mxb_qgemm({M}x{K}x{N}, bits={bits})")
+    return c_packed, c_scales, c_f32
+
+
+def linear_wonly(x: torch.Tensor, w_packed: torch.Tensor, w_scales: torch.Tensor, K: int,
+                 N: int, dt, block: int, mode: int = L.MODE_PARITY,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y[M, N] fp32 = fp32(x[M, K]) @ dequant(W^T) (mxtorch.py:7454-7473)."""
+    dt = get_mx_dtype(dt)
+    _check_dtype(dt)
+    L.require_cuda(w_packed, "linear_wonly")
+    dev = w_packed.device
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float()
+    x = x.to(dev).contiguous()
+    M = x.numel() // K
+    y = out if out is not None else torch.empty(M, N, dtype=torch.float32, device=dev)
+    lib = L.load()
+    wsb = lib.mxb_linear_wonly_workspace_size(M, K, N, dt.bits, _kind(dt), block, mode)
+    ws = L.workspace(wsb, dev)
+    in_t = L.BF16 if x.dtype == torch.bfloat16 else L.F32
+    with torch.cuda.device(dev):
+        rc = lib.mxb_linear_wonly(L.ptr(x), in_t, M, K, L.ptr(w_packed), L.ptr(w_scales), N,
+                                  dt.bits, _kind(dt), block, mode, L.ptr(y), L.ptr(ws), wsb,
+                                  L.stream_of(dev))
+    L.check(rc, f"mxb_linear_wonly({M}x{K}x{N}, {dt.name})")
+    return y

@@ -1,0 +1,148 @@
+"""CUDA path vs the reference's outputs (golden fixtures) and the oracle.
+
+Bit-exact: packed codes, scales, dequantized values, the matmul's int32
+K-block partials, fp32 accumulator and requantized codes.  Weight-only
+linear (fp32 output): |y - y64| <= 1e-5 * (|x| @ |W|) per element.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import qtpytorch_b200 as mxb
+from oracle import mx_oracle as O
+from qtpytorch_b200 import ops
+from qtpytorch_b200.dtypes import get_mx_dtype
+
+pytestmark = pytest.mark.gpu
+
+LIN_TOL = 1e-5  # per element, relative to |x| @ |W_dq|
+
+
+def _u32(a):
+    return np.ascontiguousarray(a).view(np.uint32)
+
+
+@pytest.mark.parametrize("c", cases.QUANT_CASES, ids=lambda c: c["key"])
+def test_quantize_bit_exact(golden, c):
+    dt = get_mx_dtype(c["dtype"])
+    x = cases.make_input(c).cuda()
+    q = mxb.mx_tensor.quantize(x, dt, c["block"])
+    k = c["key"]
+    assert q._mx_n == int(golden[f"{k}/n"])
+    assert np.array_equal(_u32(q._mx_scales.cpu().numpy()), _u32(golden[f"{k}/scales"]))
+    assert np.array_equal(q._mx_packed.cpu().numpy(), golden[f"{k}/packed"])
+    dq = q.dequantize()
+    assert dq.shape == x.shape
+    if f"{k}/dequant" in golden:
+        assert np.array_equal(_u32(dq.cpu().numpy()), _u32(golden[f"{k}/dequant"]))
+    else:
+        ref = O.dequantize(golden[f"{k}/packed"], golden[f"{k}/scales"], dt.bits, dt.kind,
+                           tuple(x.shape), c["block"])
+        assert np.array_equal(_u32(dq.cpu().numpy()), _u32(ref))
+
+
+@pytest.mark.parametrize("offset", [1, 3])
+def test_quantize_unaligned_views(offset):
+    # pointers not 16-byte aligned take the scalar-load path
+    base = torch.randn(4 * 256 + offset, device="cuda")
+    x = base[offset:]
+    for dt in ("int8d", "int4d", "float4d"):
+        d = get_mx_dtype(dt)
+        q = mxb.mx_tensor.quantize(x, d, 128)
+        p, s, _ = O.quantize(x.cpu().numpy(), d.bits, d.kind, 128)
+        assert np.array_equal(q._mx_packed.cpu().numpy(), p)
+        assert np.array_equal(q._mx_scales.cpu().numpy(), s)
+
+
+def test_quantize_specials():
+    x = torch.randn(8, 128)
+    x[0, 3] = float("inf")
+    x[1, :] = 0.0
+    x[2, 5] = -0.0
+    x[3, :] = 1e-30
+    for dt in ("int8d", "int4d", "int2d", "int1d", "float4d"):
+        d = get_mx_dtype(dt)
+        q = mxb.mx_tensor.quantize(x.cuda(), d, 128)
+        p, s, _ = O.quantize(x.numpy(), d.bits, d.kind, 128)
+        assert np.array_equal(q._mx_packed.cpu().numpy(), p), dt
+        assert np.array_equal(_u32(q._mx_scales.cpu().numpy()), _u32(s)), dt
+
+
+@pytest.mark.parametrize("c", [c for c in cases.QUANT_CASES if "h_" in c["key"]],
+                         ids=lambda c: c["key"])
+def test_hadamard_rotation_matches_reference(golden, c):
+    dt = get_mx_dtype(c["dtype"])
+    x = cases.make_input(c).float()
+    k = c["key"]
+    if f"{k}/rotated" not in golden:
+        pytest.skip("rotation not stored for this size")
+    xr = x if x.dim() >= 2 else x.reshape(1, -1)
+    y = ops.hadamard_rows(xr.cuda(), dt.hadamard_seed, inverse=False)
+    assert np.array_equal(_u32(y.cpu().numpy()), _u32(golden[f"{k}/rotated"]))
+
+
+def test_hadamard_roundtrip_8192():
+    # config-4 row length: unrotate(rotate(x)) == x to fp32 rounding
+    x = torch.randn(16, 8192, device="cuda")
+    y = ops.hadamard_rows(x, 1214670534, inverse=False)
+    z = ops.hadamard_rows(y, 1214670534, inverse=True)
+    assert torch.allclose(z, x, atol=1e-5, rtol=1e-5)
+    r = O.rotate(x.cpu().numpy(), mxb.sign_vector(8192, 1214670534).numpy())
+    assert np.array_equal(_u32(y.cpu().numpy()), _u32(r))
+
+
+@pytest.mark.parametrize("c", cases.GEMM_CASES, ids=lambda c: c["key"])
+def test_qgemm_bit_exact(golden, c):
+    dt = get_mx_dtype(c["dtype"])
+    a, b = cases.make_gemm_inputs(c)
+    qa = mxb.mx_tensor.quantize(a.cuda(), dt, c["block"])
+    qb = mxb.mx_tensor.quantize(b.cuda(), dt, c["block"])
+    qc = qa @ qb
+    k = c["key"]
+    assert qc._mx_dtype.bits == int(golden[f"{k}/c_bits"])
+    assert qc._mx_block == int(golden[f"{k}/c_block"])
+    assert np.array_equal(_u32(qc._mx_scales.cpu().numpy()), _u32(golden[f"{k}/c_scales"]))
+    assert np.array_equal(qc._mx_packed.cpu().numpy(), golden[f"{k}/c_packed"])
+    assert np.array_equal(_u32(qc.dequantize().cpu().numpy()), _u32(golden[f"{k}/c_dequant"]))
+
+
+def _linear_check(y, x, wdq, tol=LIN_TOL):
+    y64, bound = O.linear_ref64(x, wdq)
+    err = np.abs(y.astype(np.float64) - y64)
+    assert np.all(err <= tol * bound + 1e-30), float((err / (bound + 1e-30)).max())
+    return float((err / (bound + 1e-30)).max())
+
+
+@pytest.mark.parametrize("c", cases.LINEAR_CASES, ids=lambda c: c["key"])
+def test_mx_linear_matches_reference(golden, c):
+    lin, x = cases.make_linear_inputs(c)
+    dt = get_mx_dtype(c["dtype"])
+    ml = mxb.mx_linear.from_linear(lin.cuda(), dt, c["block"])
+    assert np.array_equal(ml._mx_weight._mx_packed.cpu().numpy(), golden[f"{c['key']}/w_packed"])
+    y = ml(x.cuda())
+    assert y.dtype == torch.float32 and y.shape == (c["M"], c["out"])
+    wdq = O.dequantize(golden[f"{c['key']}/w_packed"], golden[f"{c['key']}/w_scales"], dt.bits,
+                       dt.kind, (c["in"], c["out"]), c["block"])
+    _linear_check(y.cpu().numpy(), x.float().numpy(), wdq)
+    # the reference's own fp32 output agrees to the same tolerance
+    yr = golden[f"{c['key']}/y"]
+    y64, bound = O.linear_ref64(x.float().numpy(), wdq)
+    assert np.all(np.abs(yr - y64) <= LIN_TOL * bound + 1e-30)
+
+
+@pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 128])
+@pytest.mark.parametrize("dt", ["int4d", "int8d", "int2d", "int1d", "float4d"])
+def test_linear_shapes(M, dt):
+    d = get_mx_dtype(dt)
+    g = torch.Generator().manual_seed(M)
+    w = torch.randn(384, 256, generator=g) * 0.02   # out=384, in=256
+    x = torch.randn(M, 256, generator=g).bfloat16()
+    lin = torch.nn.Linear(256, 384, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    ml = mxb.mx_linear.from_linear(lin.cuda(), d, 128)
+    y = ml(x.cuda()).cpu().numpy()
+    pw, sw, _ = O.quantize(w.t().contiguous().numpy(), d.bits, d.kind, 128)
+    wdq = O.dequantize(pw, sw, d.bits, d.kind, (256, 384), 128)
+    _linear_check(y, x.float().numpy(), wdq)
