@@ -98,11 +98,14 @@ class Clocks:
 
 def time_steps(fn, steps, flush, stream=None):
     """Device time of each call (CUDA events on the launching stream); L2
-    flushed before each timed call."""
+    flushed before each timed call.  A short device-side sleep after the flush
+    lets the host enqueue the call before the GPU reaches the start event, so
+    the interval holds the call's kernels and not Python launch overhead."""
     st = stream or torch.cuda.current_stream()
     ts = []
     for _ in range(steps):
         flush()
+        torch.cuda._sleep(400_000)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
@@ -240,6 +243,12 @@ def run_ours(args, world, rank, local):
         step()
         gemm_only()
     barrier(world)
+    if args.only == "gemm":  # profiling case: the GEMM kernel alone, no timing
+        for _ in range(args.steps):
+            gemm_only()
+        torch.cuda.synchronize()
+        print(json.dumps({"only": "gemm", "device_error": lib.mxb_device_error(1)}))
+        return
 
     n0 = lib.mxb_launch_count()
     with Clocks(local) as clk:
@@ -369,6 +378,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true")
+    ap.add_argument("--only", default=None, choices=["gemm"],
+                    help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

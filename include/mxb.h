@@ -59,6 +59,12 @@ int mxb_version(void);
 /* Text of the last CUDA error seen by this thread ("" if none). */
 const char* mxb_last_error(void);
 
+/* Device-side error word of the current device: 0 if no kernel of this library
+ * recorded a failure, else the code of the first bounded wait that gave up
+ * (the kernel then returned early; its outputs are invalid).  Synchronises
+ * the device.  clear != 0 resets the word. */
+int mxb_device_error(int clear);
+
 /* Number of kernels this library has launched in this process (all threads). */
 uint64_t mxb_launch_count(void);
 

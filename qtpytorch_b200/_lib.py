@@ -36,6 +36,7 @@ PROTOTYPES = {
     "mxb_version": (_int, []),
     "mxb_last_error": (C.c_char_p, []),
     "mxb_launch_count": (C.c_uint64, []),
+    "mxb_device_error": (_int, [_int]),
     "mxb_packed_bytes": (_sz, [_i64, _int, _int]),
     "mxb_quantize_workspace_size": (_sz, [_i64, _i64, _int, _int, _int, _int]),
     "mxb_quantize": (_int, [_vp, _int, _i64, _i64, _int, _int, _int, _int, _vp, _vp, _vp,

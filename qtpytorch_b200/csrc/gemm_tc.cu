@@ -1,17 +1,303 @@
-// tcgen05 GEMM kernels (placeholder: routing disabled until the kernels land).
+// tcgen05 packed integer GEMM for sm_100a (int8 codes, kind::i8).
+//
+// C = sum over K-blocks kb of fl(fl(P_kb * sa[m, kb]) * sb[kb, n]), in kb
+// order, P_kb the exact int32 product of one 128-wide K-block
+// (mxtorch.py:1299-1385).  One CTA owns a 128x128 tile of C:
+//   warp 0      TMA producer: A [128 x 128 B] (K-major) and B [128 K x 128 N]
+//               (N-major, B's native row-major layout) per K-block, 128-byte
+//               swizzle, STAGES-deep ring of shared-memory stages;
+//   warp 1      allocates 256 TMEM columns and issues 4 x tcgen05.mma
+//               (M=128, N=128, K=32, s8 x s8 -> s32) per K-block into one of
+//               two TMEM accumulators, so the MMAs of K-block kb+1 overlap
+//               the promotion of kb;
+//   warps 2..9  promotion: tcgen05.ld the int32 tile (one TMEM lane = one
+//               row, 64 columns per warp), convert exactly, apply both
+//               scales and add into fp32 registers with one rounding per
+//               step.  The fp32 accumulator is bit-identical to the
+//               reference's.
+// Sub-byte codes (int4 / int2 / int1) are first widened to int8 in the
+// workspace.  All waits are bounded (tc_ptx.cuh).
 #include "mxb_common.cuh"
 #include "mxb_internal.h"
 
+#include <cuda.h>
+
+namespace mxb {
+__device__ int g_mxb_device_error = 0;
+}
+
+#include "tc_ptx.cuh"
+
 namespace mxb {
 
-bool tc_qgemm_eligible(int64_t, int64_t, int64_t, int, int, bool, bool, const void*,
-                       const void*, const float*) {
-  return false;
+namespace {
+
+constexpr int BM = 128, BN = 128, BKB = 128;  // tile rows, cols, K-block bytes
+constexpr int STAGES = 4;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kTileA = BM * BKB;   // 16 KB
+constexpr int kTileB = BN * BKB;   // 16 KB
+constexpr int kTmemCols = 2 * BN;  // two int32 accumulators
+constexpr size_t kSmemBytes = 1024 + (size_t)STAGES * (kTileA + kTileB) + 256;
+
+struct Bars {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t done;
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b, const float* __restrict__ sa,
+                    const float* __restrict__ sb, int M, int N, int K, float* __restrict__ C) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kTileA;
+  Bars* bars = reinterpret_cast<Bars*>(sB + STAGES * kTileB);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int kbn = K / BKB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->tfull[b], 1);
+      mbar_init(&bars->tempty[b], kEpiWarps);
+    }
+    mbar_init(&bars->done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < kbn; ++kb) {
+        const int s = kb % STAGES, round = kb / STAGES;
+        if (round > 0 && !mbar_wait(&bars->empty[s], (round - 1) & 1, kErrTimeoutEmpty)) break;
+        mbar_expect_tx(&bars->full[s], kTileA + kTileB);
+        tma_load_2d(sA + s * kTileA, &tmap_a, &bars->full[s], kb * BKB, m0);
+        tma_load_2d(sB + s * kTileB, &tmap_b, &bars->full[s], n0, kb * BKB);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(/*S32*/ 2, /*s8*/ 1, 0, /*B N-major*/ 1, BM, BN);
+      for (int kb = 0; kb < kbn; ++kb) {
+        const int s = kb % STAGES, round = kb / STAGES;
+        const int b = kb & 1, use = kb >> 1;
+        if (!mbar_wait(&bars->full[s], round & 1, kErrTimeoutFull)) break;
+        if (use > 0 && !mbar_wait(&bars->tempty[b], (use - 1) & 1, kErrTimeoutTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + s * kTileA), b0 = smem_u32(sB + s * kTileB);
+#pragma unroll
+        for (int kk = 0; kk < BKB / 32; ++kk) {
+          mma_i8(tbase + b * BN, desc_kmajor_sw128(a0 + kk * 32),
+                 desc_mnmajor_sw128(b0 + kk * 32 * BN, kTileB), idesc, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&bars->empty[s]);
+        mma_commit(&bars->tfull[b]);
+      }
+      mma_commit(&bars->done);
+    }
+  } else {
+    const int ew = warp - 2;
+    const int q = warp & 3;          // TMEM lane quadrant this warp may access
+    const int col0 = (ew >> 2) * 64;  // column half
+    const int row = q * 32 + lane;
+    const int m = m0 + row;
+    float acc[64];
+#pragma unroll
+    for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
+    const float* sap = sa + (size_t)m * kbn;
+    float sa_next = __ldg(sap);
+    for (int kb = 0; kb < kbn; ++kb) {
+      const int b = kb & 1, use = kb >> 1;
+      const float sa_v = sa_next;
+      if (kb + 1 < kbn) sa_next = __ldg(sap + kb + 1);
+      if (!mbar_wait_warp(&bars->tfull[b], use & 1, kErrTimeoutTmemFull)) break;
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16) + b * BN + col0;
+      tmem_ld32(taddr, r0);
+      tmem_ld32(taddr + 32, r1);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->tempty[b]);
+      const float4* sbp = reinterpret_cast<const float4*>(sb + (size_t)kb * N + n0 + col0);
+#pragma unroll
+      for (int c4 = 0; c4 < 16; ++c4) {
+        const float4 s4 = __ldg(sbp + c4);
+        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = c4 * 4 + j;
+          const int p = (int)(c < 32 ? r0[c] : r1[c - 32]);
+          acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(__int2float_rn(p), sa_v), sv[j]));
+        }
+      }
+    }
+    float4* out = reinterpret_cast<float4*>(C + (size_t)m * N + n0 + col0);
+#pragma unroll
+    for (int c4 = 0; c4 < 16; ++c4)
+      out[c4] = make_float4(acc[4 * c4], acc[4 * c4 + 1], acc[4 * c4 + 2], acc[4 * c4 + 3]);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    mbar_wait(&bars->done, 0, kErrTimeoutDone);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
 }
-size_t tc_qgemm_workspace(int64_t, int64_t, int64_t, int) { return 0; }
-int tc_qgemm(const void*, const float*, const void*, const float*, int64_t, int64_t, int64_t,
-             int, int, float*, void*, size_t, cudaStream_t) {
-  return MXB_E_SHAPE;
+
+// Widen packed sub-byte codes to one signed byte per code.
+template <int BITS>
+__global__ void __launch_bounds__(256) widen_codes_kernel(const uint8_t* __restrict__ p,
+                                                          int64_t n, int8_t* __restrict__ out) {
+  constexpr int PER = 8 / BITS;
+  const int64_t nbytes = (n + PER - 1) / PER;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nbytes;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t b = p[i];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int64_t e = i * PER + j;
+      if (e < n) out[e] = (int8_t)sext((b >> (j * BITS)) & ((1u << BITS) - 1u), BITS);
+    }
+  }
+}
+
+int widen(const void* p, int64_t n, int bits, int8_t* out, cudaStream_t st) {
+  const int per = 8 / bits;
+  int64_t g = cdiv(cdiv(n, per), 256);
+  if (g > kSMs * 16) g = kSMs * 16;
+  const uint8_t* src = static_cast<const uint8_t*>(p);
+  switch (bits) {
+    case 1: widen_codes_kernel<1><<<(unsigned)g, 256, 0, st>>>(src, n, out); break;
+    case 2: widen_codes_kernel<2><<<(unsigned)g, 256, 0, st>>>(src, n, out); break;
+    case 4: widen_codes_kernel<4><<<(unsigned)g, 256, 0, st>>>(src, n, out); break;
+    default: return MXB_E_DTYPE;
+  }
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// 2-D row-major byte matrix [rows][cols] -> tensor map with a 128x128-byte box,
+// 128-byte swizzle.
+int make_tmap_u8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                 uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return MXB_E_CUDA;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                   box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MXB_OK : MXB_E_CUDA;
+}
+
+bool tc_qgemm_eligible(int64_t M, int64_t K, int64_t N, int bits, int block, bool sa_ok,
+                       bool sb_ok, const void* a, const void* b, const float* c) {
+  if (block != BKB || !sa_ok || !sb_ok) return false;
+  if (bits != 8 && bits != 4 && bits != 2 && bits != 1) return false;
+  if (M % BM || N % BN || K % BKB || M <= 0 || N <= 0 || K <= 0) return false;
+  if (bits == 8 && (((uintptr_t)a | (uintptr_t)b) & 15)) return false;
+  if ((uintptr_t)c & 15) return false;
+  return true;
+}
+
+size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits) {
+  if (bits == 8) return 0;
+  return (size_t)((M * K + 255) / 256 * 256 + (K * N + 255) / 256 * 256);
+}
+
+int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
+             int64_t K, int64_t N, int bits, int block, float* C, void* ws, size_t wsb,
+             cudaStream_t st) {
+  (void)block;
+  const void* a8 = a;
+  const void* b8 = b;
+  if (bits != 8) {
+    if (wsb < tc_qgemm_workspace(M, K, N, bits)) return MXB_E_WORKSPACE;
+    int8_t* wa = static_cast<int8_t*>(ws);
+    int8_t* wb = wa + (M * K + 255) / 256 * 256;
+    int rc = widen(a, M * K, bits, wa, st);
+    if (rc != MXB_OK) return rc;
+    rc = widen(b, K * N, bits, wb, st);
+    if (rc != MXB_OK) return rc;
+    a8 = wa;
+    b8 = wb;
+  }
+  CUtensorMap ta, tb;
+  if (make_tmap_u8(&ta, a8, (uint64_t)K, (uint64_t)M, BKB, BM) != MXB_OK) return MXB_E_CUDA;
+  if (make_tmap_u8(&tb, b8, (uint64_t)N, (uint64_t)K, BN, BKB) != MXB_OK) return MXB_E_CUDA;
+  static bool attr_set = false;
+  if (!attr_set) {
+    MXB_CUDA_TRY(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kSmemBytes));
+    attr_set = true;
+  }
+  dim3 grid((unsigned)(N / BN), (unsigned)(M / BM));
+  qgemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
 }
 
 }  // namespace mxb
+
+extern "C" int mxb_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, mxb::g_mxb_device_error, sizeof(int)) != cudaSuccess)
+    return MXB_E_CUDA;
+  if (clear && v != 0) {
+    int z = 0;
+    if (cudaMemcpyToSymbol(mxb::g_mxb_device_error, &z, sizeof(int)) != cudaSuccess)
+      return MXB_E_CUDA;
+  }
+  return v;
+}

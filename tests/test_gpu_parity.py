@@ -37,8 +37,11 @@ def test_quantize_bit_exact(golden, c):
     if f"{k}/dequant" in golden:
         assert np.array_equal(_u32(dq.cpu().numpy()), _u32(golden[f"{k}/dequant"]))
     else:
+        signs = None
+        if dt.is_hadamard:
+            signs = mxb.sign_vector(ops.row_len_of(x.shape), dt.hadamard_seed).numpy()
         ref = O.dequantize(golden[f"{k}/packed"], golden[f"{k}/scales"], dt.bits, dt.kind,
-                           tuple(x.shape), c["block"])
+                           tuple(x.shape), c["block"], dt.is_hadamard, signs)
         assert np.array_equal(_u32(dq.cpu().numpy()), _u32(ref))
 
 
