@@ -39,7 +39,8 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kTileA = BM * BKB;   // 16 KB
 constexpr int kTileB = BN * BKB;   // 16 KB
 constexpr int kTmemCols = 2 * BN;  // two int32 accumulators
-constexpr size_t kSmemBytes = 1024 + (size_t)STAGES * (kTileA + kTileB) + 256;
+constexpr size_t kBarsBytes = 4096 + 512;  // >= sizeof(Bars), checked below
+constexpr size_t kSmemBytes = 1024 + (size_t)STAGES * (kTileA + kTileB) + kBarsBytes;
 
 struct Bars {
   uint64_t full[STAGES];
@@ -48,7 +49,11 @@ struct Bars {
   uint64_t tempty[2];
   uint64_t done;
   uint32_t tmem_base;
+  // per-warp double buffer of B scales, read back as float4 broadcasts
+  alignas(16) float sbw[kEpiWarps][2 * 64];
 };
+static_assert(sizeof(Bars) <= kBarsBytes, "barrier block overflows its shared-memory slot");
+static_assert(offsetof(Bars, sbw) % 16 == 0, "float4 reads of sbw need 16-byte alignment");
 
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -129,12 +134,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     float acc[64];
 #pragma unroll
     for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
+    // Scales are fetched one K-block ahead: sa (one per row) into a register,
+    // this warp's 64 sb values two per lane, staged through a per-warp
+    // double buffer in shared memory and read back as broadcasts.
+    float* sbw = bars->sbw[ew];
     const float* sap = sa + (size_t)m * kbn;
+    const float* sbrow = sb + n0 + col0 + 2 * lane;
     float sa_next = __ldg(sap);
+    float2 sb_next = __ldg(reinterpret_cast<const float2*>(sbrow));
     for (int kb = 0; kb < kbn; ++kb) {
       const int b = kb & 1, use = kb >> 1;
       const float sa_v = sa_next;
-      if (kb + 1 < kbn) sa_next = __ldg(sap + kb + 1);
+      reinterpret_cast<float2*>(sbw + b * 64)[lane] = sb_next;
+      __syncwarp();
+      if (kb + 1 < kbn) {
+        sa_next = __ldg(sap + kb + 1);
+        sb_next = __ldg(reinterpret_cast<const float2*>(sbrow + (size_t)(kb + 1) * N));
+      }
       if (!mbar_wait_warp(&bars->tfull[b], use & 1, kErrTimeoutTmemFull)) break;
       tc_fence_after();
       uint32_t r0[32], r1[32];
@@ -145,16 +161,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty[b]);
-      const float4* sbp = reinterpret_cast<const float4*>(sb + (size_t)kb * N + n0 + col0);
+      const float4* sbp = reinterpret_cast<const float4*>(sbw + b * 64);
 #pragma unroll
       for (int c4 = 0; c4 < 16; ++c4) {
-        const float4 s4 = __ldg(sbp + c4);
+        const float4 s4 = sbp[c4];
         const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int c = c4 * 4 + j;
           const int p = (int)(c < 32 ? r0[c] : r1[c - 32]);
-          acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(__int2float_rn(p), sa_v), sv[j]));
+          // exact int -> fp32 for |p| < 2^22: 1.5 * 2^23 + p holds p in its
+          // low mantissa bits; |P| <= 128 * 127^2 < 2^22
+          const float pf = __fsub_rn(__int_as_float(0x4B400000 + p), 12582912.0f);
+          acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(pf, sa_v), sv[j]));
         }
       }
     }

@@ -64,9 +64,11 @@ __device__ __forceinline__ int f4_bucket(float v) {
               m10 = __uint_as_float(0x3e555556u), m11 = __uint_as_float(0x3e955556u),
               m12 = __uint_as_float(0x3ed55556u), m13 = __uint_as_float(0x3f155556u),
               m14 = __uint_as_float(0x3f555556u);
-  int i = (v > m0) + (v > m1) + (v > m2) + (v > m3) + (v > m4) + (v > m5) + (v > m6) +
-          (v > m7) + (v > m8) + (v > m9) + (v > m10) + (v > m11) + (v > m12) +
-          (v > m13) + (v > m14);
+  // !(v <= m) == (v > m) for numbers; NaN counts past every boundary (-> 15),
+  // as torch.bucketize places NaN last
+  int i = !(v <= m0) + !(v <= m1) + !(v <= m2) + !(v <= m3) + !(v <= m4) + !(v <= m5) +
+          !(v <= m6) + !(v <= m7) + !(v <= m8) + !(v <= m9) + !(v <= m10) + !(v <= m11) +
+          !(v <= m12) + !(v <= m13) + !(v <= m14);
   return i;
 }
 
