@@ -10,9 +10,9 @@
 //               (M=128, N=128, K=32, s8 x s8 -> s32) per K-block into one of
 //               two TMEM accumulators, so the MMAs of K-block kb+1 overlap
 //               the promotion of kb;
-//   warps 2..9  promotion: tcgen05.ld the int32 tile (one TMEM lane = one
-//               row, 64 columns per warp), convert exactly, apply both
-//               scales and add into fp32 registers with one rounding per
+//   warps 2..17 promotion: tcgen05.ld the int32 tile (one TMEM lane = one
+//               row, 32 columns per warp), convert exactly, apply both
+//               scales and add into fp32 registers (packed f32x2 ops), one rounding per
 //               step.  The fp32 accumulator is bit-identical to the
 //               reference's.
 // Sub-byte codes (int4 / int2 / int1) are first widened to int8 in the
@@ -34,7 +34,9 @@ namespace {
 
 constexpr int BM = 128, BN = 128, BKB = 128;  // tile rows, cols, K-block bytes
 constexpr int STAGES = 4;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
+constexpr int kEpiCols = BN * 4 / kEpiWarps;  // columns per epilogue warp (32)
+static_assert(kEpiCols == 32, "one tcgen05.ld x32 per warp and K-block");
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kTileA = BM * BKB;   // 16 KB
 constexpr int kTileB = BN * BKB;   // 16 KB
@@ -50,7 +52,7 @@ struct Bars {
   uint64_t done;
   uint32_t tmem_base;
   // per-warp double buffer of B scales, read back as float4 broadcasts
-  alignas(16) float sbw[kEpiWarps][2 * 64];
+  alignas(16) float sbw[kEpiWarps][2 * kEpiCols];
 };
 static_assert(sizeof(Bars) <= kBarsBytes, "barrier block overflows its shared-memory slot");
 static_assert(offsetof(Bars, sbw) % 16 == 0, "float4 reads of sbw need 16-byte alignment");
@@ -127,60 +129,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int ew = warp - 2;
-    const int q = warp & 3;          // TMEM lane quadrant this warp may access
-    const int col0 = (ew >> 2) * 64;  // column half
+    const int q = warp & 3;                 // TMEM lane quadrant this warp may access
+    const int col0 = (ew >> 2) * kEpiCols;  // this warp's column slice
     const int row = q * 32 + lane;
     const int m = m0 + row;
-    float acc[64];
+    // fp32 accumulator as packed pairs (f32x2 ops round each lane like the
+    // scalar op, so results stay bit-identical)
+    uint64_t acc[kEpiCols / 2];
 #pragma unroll
-    for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
+    for (int c = 0; c < kEpiCols / 2; ++c) acc[c] = 0ull;
     // Scales are fetched one K-block ahead: sa (one per row) into a register,
-    // this warp's 64 sb values two per lane, staged through a per-warp
+    // this warp's sb slice one value per lane, staged through a per-warp
     // double buffer in shared memory and read back as broadcasts.
     float* sbw = bars->sbw[ew];
     const float* sap = sa + (size_t)m * kbn;
-    const float* sbrow = sb + n0 + col0 + 2 * lane;
+    const float* sbrow = sb + n0 + col0 + lane;
     float sa_next = __ldg(sap);
-    float2 sb_next = __ldg(reinterpret_cast<const float2*>(sbrow));
+    float sb_next = __ldg(sbrow);
+    const uint64_t magic2 = pack2(12582912.0f, 12582912.0f);
     for (int kb = 0; kb < kbn; ++kb) {
       const int b = kb & 1, use = kb >> 1;
       const float sa_v = sa_next;
-      reinterpret_cast<float2*>(sbw + b * 64)[lane] = sb_next;
+      sbw[b * kEpiCols + lane] = sb_next;
       __syncwarp();
       if (kb + 1 < kbn) {
         sa_next = __ldg(sap + kb + 1);
-        sb_next = __ldg(reinterpret_cast<const float2*>(sbrow + (size_t)(kb + 1) * N));
+        sb_next = __ldg(sbrow + (size_t)(kb + 1) * N);
       }
       if (!mbar_wait_warp(&bars->tfull[b], use & 1, kErrTimeoutTmemFull)) break;
       tc_fence_after();
-      uint32_t r0[32], r1[32];
+      uint32_t r[kEpiCols];
       const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16) + b * BN + col0;
-      tmem_ld32(taddr, r0);
-      tmem_ld32(taddr + 32, r1);
+      tmem_ld32(taddr, r);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->tempty[b]);
-      const float4* sbp = reinterpret_cast<const float4*>(sbw + b * 64);
+      const uint64_t sa2 = pack2(sa_v, sa_v);
+      const ulonglong2* sbp = reinterpret_cast<const ulonglong2*>(sbw + b * kEpiCols);
 #pragma unroll
-      for (int c4 = 0; c4 < 16; ++c4) {
-        const float4 s4 = sbp[c4];
-        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+      for (int c4 = 0; c4 < kEpiCols / 4; ++c4) {
+        const ulonglong2 s4 = sbp[c4];
+        const uint64_t sv[2] = {s4.x, s4.y};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = c4 * 4 + j;
-          const int p = (int)(c < 32 ? r0[c] : r1[c - 32]);
+        for (int j = 0; j < 2; ++j) {
+          const int c = c4 * 4 + 2 * j;
           // exact int -> fp32 for |p| < 2^22: 1.5 * 2^23 + p holds p in its
           // low mantissa bits; |P| <= 128 * 127^2 < 2^22
-          const float pf = __fsub_rn(__int_as_float(0x4B400000 + p), 12582912.0f);
-          acc[c] = __fadd_rn(acc[c], __fmul_rn(__fmul_rn(pf, sa_v), sv[j]));
+          const uint64_t biased = pack2(__int_as_float(0x4B400000 + (int)r[c]),
+                                        __int_as_float(0x4B400000 + (int)r[c + 1]));
+          const uint64_t pf = fsub2(biased, magic2);
+          acc[c / 2] = fadd2(acc[c / 2], fmul2(fmul2(pf, sa2), sv[j]));
         }
       }
     }
     float4* out = reinterpret_cast<float4*>(C + (size_t)m * N + n0 + col0);
 #pragma unroll
-    for (int c4 = 0; c4 < 16; ++c4)
-      out[c4] = make_float4(acc[4 * c4], acc[4 * c4 + 1], acc[4 * c4 + 2], acc[4 * c4 + 3]);
+    for (int c4 = 0; c4 < kEpiCols / 4; ++c4) {
+      const float2 lo = unpack2(acc[2 * c4]), hi = unpack2(acc[2 * c4 + 1]);
+      out[c4] = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
   }
   __syncthreads();
   if (warp == 1) {
