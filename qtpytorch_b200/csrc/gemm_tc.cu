@@ -179,7 +179,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t biased = pack2(__int_as_float(0x4B400000 + (int)r[c]),
                                         __int_as_float(0x4B400000 + (int)r[c + 1]));
           const uint64_t pf = fsub2(biased, magic2);
-          acc[c / 2] = fadd2(acc[c / 2], fmul2(fmul2(pf, sa2), sv[j]));
+          // products packed; the add stays scalar so it is never fused
+          // with the multiply (a fused add would skip one rounding)
+          const float2 t = unpack2(fmul2(fmul2(pf, sa2), sv[j]));
+          const float2 a = unpack2(acc[c / 2]);
+          acc[c / 2] = pack2(__fadd_rn(a.x, t.x), __fadd_rn(a.y, t.y));
         }
       }
     }
