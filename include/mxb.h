@@ -159,6 +159,28 @@ int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const voi
                      int mode, float* y, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/*
+ * The decode (M <= 16) weight-only linear of mxb_linear_wonly, for callers
+ * that cannot allocate device memory when they run the layer: runtimes that
+ * only use buffers planned ahead of time, code inside a fixed memory pool,
+ * or foreign-language hosts without a CUDA allocator.  It takes no
+ * workspace; the split-K partial sums go to a 16 MiB array inside the
+ * library (every GPU that loads the library keeps it until exit).
+ * It has no counterpart in the reference; it exists only for such callers.
+ *   Same arguments and result as mxb_linear_wonly for the GEMV shapes
+ *   (1 <= M <= 16, N % 8 == 0, N % block == 0, block % 8 == 0); other shapes
+ *   return MXB_E_SHAPE.  Shapes whose partial sums cannot fit 16 MiB even
+ *   with 256-row K splits (splits * M * N * 4 bytes) return MXB_E_WORKSPACE.
+ *   The first call on each device looks the array up (with that device
+ *   current); make that first call before any stream capture.  All calls
+ *   share the array: calls that may run at the same time on the GPU (other
+ *   streams, other threads) race and must be serialized by the caller.
+ *   Nothing in it needs clearing: each call writes every partial sum it reads.
+ */
+int mxb_linear_wonly_noalloc(const void* x, int x_dtype, int64_t M, int64_t K,
+                             const void* w_packed, const float* w_scales, int64_t N, int bits,
+                             int kind, int block, float* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

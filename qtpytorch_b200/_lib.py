@@ -37,6 +37,8 @@ PROTOTYPES = {
     "mxb_last_error": (C.c_char_p, []),
     "mxb_launch_count": (C.c_uint64, []),
     "mxb_device_error": (_int, [_int]),
+    "mxb_linear_wonly_noalloc": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _i64, _int, _int, _int,
+                                        _vp, _vp]),
     "mxb_packed_bytes": (_sz, [_i64, _int, _int]),
     "mxb_quantize_workspace_size": (_sz, [_i64, _i64, _int, _int, _int, _int]),
     "mxb_quantize": (_int, [_vp, _int, _i64, _i64, _int, _int, _int, _int, _vp, _vp, _vp,

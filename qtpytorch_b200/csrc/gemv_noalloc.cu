@@ -1,0 +1,85 @@
+// Decode-regime weight-only linear without any caller-supplied workspace.
+//
+// mxb_linear_wonly needs a workspace for the split-K partial sums, which the
+// caller allocates.  Some callers cannot allocate device memory at the point
+// where they run the layer: a host runtime that only hands out buffers it
+// planned ahead of time, code running inside a pre-sized memory pool, or an
+// FFI caller (Go, Java, ...) that has no CUDA allocator of its own.  This
+// variant keeps the partial sums in a fixed array that lives in the library
+// itself, so the caller passes only x, the packed weight and y.
+#include "mxb_common.cuh"
+#include "mxb_internal.h"
+
+#include <mutex>
+
+namespace {
+
+// Partial-sum scratch shared by every call on a device: 16 MiB.  Each GPU
+// that loads the library holds it until the process exits.
+constexpr size_t kScratchBytes = 16u << 20;
+static __device__ __align__(256) float g_gemv_scratch[kScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxRowsPerSplit = 256;  // the split-K kernel's shared x slice
+
+// Device address of g_gemv_scratch, looked up once per device (with that
+// device current).  In host code the symbol itself is only a host-side
+// stand-in and must never be passed to a kernel.
+float* scratch_ptr(int dev, int* rc) {
+  static std::mutex mu;
+  static float* ptrs[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) {
+    *rc = MXB_E_ARG;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_scratch);
+    if (e != cudaSuccess) {
+      mxb_set_cuda_error(e);
+      *rc = MXB_E_CUDA;
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  *rc = MXB_OK;
+  return ptrs[dev];
+}
+
+}  // namespace
+
+extern "C" int mxb_linear_wonly_noalloc(const void* x, int x_dtype, int64_t M, int64_t K,
+                                        const void* w_packed, const float* w_scales, int64_t N,
+                                        int bits, int kind, int block, float* y,
+                                        void* stream) {
+  if (kind == MXB_KIND_FLOAT ? bits != 4
+                             : !(bits == 1 || bits == 2 || bits == 4 || bits == 8))
+    return MXB_E_DTYPE;
+  if (kind != MXB_KIND_INT && kind != MXB_KIND_FLOAT) return MXB_E_DTYPE;
+  if (x_dtype != MXB_F32 && x_dtype != MXB_BF16) return MXB_E_DTYPE;
+  if (M < 0 || K <= 0 || N <= 0 || block <= 0) return MXB_E_SHAPE;
+  if (M == 0) return MXB_OK;
+  if (K * N >= (int64_t)1 << 31) return MXB_E_SHAPE;
+  if (!x || !w_packed || !w_scales || !y) return MXB_E_ARG;
+
+  mxb::GemvPlan plan = mxb::gemv_plan(M, K, N, bits, kind, block, w_packed, y);
+  if (!plan.ok) return MXB_E_SHAPE;  // not a split-K GEMV shape (M <= 16 etc.)
+  // Fewer, longer K splits until the partial sums fit the fixed scratch.
+  while (plan.ws_bytes > kScratchBytes && plan.krows < kMaxRowsPerSplit) {
+    int64_t krows = plan.krows * 2 > kMaxRowsPerSplit ? kMaxRowsPerSplit : plan.krows * 2;
+    plan.krows = (int)krows;
+    plan.splits = (int)mxb::cdiv(K, krows);
+    plan.ws_bytes = (size_t)plan.splits * M * N * sizeof(float);
+  }
+  if (plan.ws_bytes > kScratchBytes) return MXB_E_WORKSPACE;  // beyond the 16 MiB maximum
+
+  int dev = 0;
+  MXB_CUDA_TRY(cudaGetDevice(&dev));
+  int rc = MXB_OK;
+  float* scratch = scratch_ptr(dev, &rc);
+  if (rc != MXB_OK) return rc;
+  // Every partial sum is written before it is read, so nothing is cleared.
+  return mxb::gemv_run(plan, x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y,
+                       scratch, static_cast<cudaStream_t>(stream));
+}
