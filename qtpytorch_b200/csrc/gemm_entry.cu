@@ -94,6 +94,8 @@ int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const voi
     return gemv_run(p, x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y,
                     static_cast<float*>(workspace), st);
   }
+  if (tc_wonly_eligible(x, x_dtype, M, K, w_packed, N, bits, kind, block, y))
+    return tc_wonly(x, M, K, w_packed, w_scales, N, bits, kind, block, mode, y, st);
   return wonly_generic(x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y, st);
 }
 

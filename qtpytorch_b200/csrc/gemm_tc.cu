@@ -27,6 +27,7 @@ __device__ int g_mxb_device_error = 0;
 }
 
 #include "tc_ptx.cuh"
+#include "wonly_tc.cuh"
 
 namespace mxb {
 
@@ -258,18 +259,26 @@ EncodeTiledFn encode_fn() {
 
 // 2-D row-major byte matrix [rows][cols] -> tensor map with a 128x128-byte box,
 // 128-byte swizzle.
-int make_tmap_u8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
-                 uint32_t box_cols, uint32_t box_rows) {
+// 2-D row-major matrix [rows][cols] of `esize`-byte elements -> tensor map.
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base,
+                 uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swz) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return MXB_E_CUDA;
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols};
+  cuuint64_t strides[1] = {cols * esize};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t elem[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                   box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, elem,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? MXB_OK : MXB_E_CUDA;
+}
+
+int make_tmap_u8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                 uint32_t box_cols, uint32_t box_rows) {
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, cols, rows, box_cols, box_rows,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool tc_qgemm_eligible(int64_t M, int64_t K, int64_t N, int bits, int block, bool sa_ok,
@@ -307,16 +316,66 @@ int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int
   CUtensorMap ta, tb;
   if (make_tmap_u8(&ta, a8, (uint64_t)K, (uint64_t)M, BKB, BM) != MXB_OK) return MXB_E_CUDA;
   if (make_tmap_u8(&tb, b8, (uint64_t)N, (uint64_t)K, BN, BKB) != MXB_OK) return MXB_E_CUDA;
-  static bool attr_set = false;
-  if (!attr_set) {
-    MXB_CUDA_TRY(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)kSmemBytes));
-    attr_set = true;
-  }
+  // set per call: the attribute belongs to the current device's context
+  MXB_CUDA_TRY(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kSmemBytes));
   dim3 grid((unsigned)(N / BN), (unsigned)(M / BM));
   qgemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C);
   MXB_LAUNCH_CHECK();
   return MXB_OK;
+}
+
+// ── weight-only GEMM (wonly_tc.cuh) ──────────────────────────────────────────
+bool tc_wonly_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
+                       int64_t N, int bits, int kind, int block, const float* y) {
+  if (x_dtype != MXB_BF16 || M <= 16) return false;
+  if (K % wo::BK || N % wo::BN || block % 8 || N % block) return false;
+  if (kind == MXB_KIND_FLOAT ? bits != 4 : !(bits == 1 || bits == 2 || bits == 4 || bits == 8))
+    return false;
+  if (((uintptr_t)x | (uintptr_t)w | (uintptr_t)y) & 15) return false;
+  return true;
+}
+
+template <int BITS, int KIND, bool FAST>
+static int wonly_launch(const CUtensorMap& tx, const CUtensorMap& tw, const float* ws, int M,
+                        int N, int K, int block, float* y, cudaStream_t st) {
+  auto kern = wo::wonly_tc_kernel<BITS, KIND, FAST>;
+  MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)wo::kSmemBytes));
+  dim3 grid((unsigned)(N / wo::BN), (unsigned)cdiv(M, wo::BM));
+  kern<<<grid, wo::kThreads, wo::kSmemBytes, st>>>(tx, tw, ws, M, N, K, block, y);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+template <int BITS, int KIND>
+static int wonly_mode(bool fast, const CUtensorMap& tx, const CUtensorMap& tw, const float* ws,
+                      int M, int N, int K, int block, float* y, cudaStream_t st) {
+  return fast ? wonly_launch<BITS, KIND, true>(tx, tw, ws, M, N, K, block, y, st)
+              : wonly_launch<BITS, KIND, false>(tx, tw, ws, M, N, K, block, y, st);
+}
+
+int tc_wonly(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
+             int bits, int kind, int block, int mode, float* y, cudaStream_t st) {
+  CUtensorMap tx, tw;
+  if (make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)K, (uint64_t)M, wo::BK,
+                   128, CU_TENSOR_MAP_SWIZZLE_128B) != MXB_OK)
+    return MXB_E_CUDA;
+  const uint64_t row_bytes = (uint64_t)N * bits / 8;
+  if (make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, row_bytes, (uint64_t)K,
+                   (uint32_t)(wo::BN * bits / 8), wo::BK, CU_TENSOR_MAP_SWIZZLE_NONE) != MXB_OK)
+    return MXB_E_CUDA;
+  const bool fast = mode == MXB_MODE_FAST;
+  const int iM = (int)M, iN = (int)N, iK = (int)K;
+  if (kind == MXB_KIND_FLOAT)
+    return wonly_mode<4, MXB_KIND_FLOAT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
+  switch (bits) {
+    case 1: return wonly_mode<1, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
+    case 2: return wonly_mode<2, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
+    case 4: return wonly_mode<4, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
+    case 8: return wonly_mode<8, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
+  }
+  return MXB_E_DTYPE;
 }
 
 }  // namespace mxb

@@ -40,5 +40,9 @@ size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits);
 int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
              int64_t K, int64_t N, int bits, int block, float* C, void* ws, size_t wsb,
              cudaStream_t st);
+bool tc_wonly_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
+                       int64_t N, int bits, int kind, int block, const float* y);
+int tc_wonly(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
+             int bits, int kind, int block, int mode, float* y, cudaStream_t st);
 
 }  // namespace mxb
