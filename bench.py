@@ -96,6 +96,19 @@ class Clocks:
                 "samples": len(sm)}
 
 
+def graphed(fn, stream):
+    """Capture fn (already warmed up) into a CUDA graph; returns a replay
+    callable, or fn itself if capture is not possible."""
+    g = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+    except Exception:  # noqa: BLE001 - fall back to eager launches
+        torch.cuda.synchronize()
+        return fn
+    return g.replay
+
+
 def time_steps(fn, steps, flush, stream=None):
     """Device time of each call (CUDA events on the launching stream); L2
     flushed before each timed call.  A short device-side sleep after the flush
@@ -105,7 +118,7 @@ def time_steps(fn, steps, flush, stream=None):
     ts = []
     for _ in range(steps):
         flush()
-        torch.cuda._sleep(400_000)
+        torch.cuda._sleep(1_000_000)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
@@ -215,6 +228,10 @@ def run_ours(args, world, rank, local):
     def flush():
         flush_buf.zero_()
 
+    if args.only in ("gemv1", "gemv16", "wo2048"):
+        print(json.dumps(run_extras(args, dev, flush, torch.cuda.current_stream(dev), hbm, bf16)))
+        return
+
     a_h, b_h = make_inputs()
     qa = mxb.mx_tensor.quantize(a_h.to(dev), mxb.int8d, BLOCK)
     qb = mxb.mx_tensor.quantize(b_h.to(dev), mxb.int8d, BLOCK)
@@ -250,16 +267,20 @@ def run_ours(args, world, rank, local):
         print(json.dumps({"only": "gemm", "device_error": lib.mxb_device_error(1)}))
         return
 
+    # kernels of this library per step, counted on one eager step; the timed
+    # steps replay the same launches from a CUDA graph
     n0 = lib.mxb_launch_count()
+    step()
+    launches = (lib.mxb_launch_count() - n0) * args.steps
+    step_g = graphed(step, stream)
     with Clocks(local) as clk:
         barrier(world)
-        ts = time_steps(step, args.steps, flush, stream)
+        ts = time_steps(step_g, args.steps, flush, stream)
         barrier(world)
-    launches = (lib.mxb_launch_count() - n0) // max(args.steps, 1) * args.steps
     step_ms = max_over_ranks(sum(ts) / len(ts), world)
     value = 2.0 * M * N * K / (step_ms * 1e-3) / 1e12
 
-    tg = time_steps(gemm_only, args.steps, flush, stream)
+    tg = time_steps(graphed(gemm_only, stream), args.steps, flush, stream)
     gemm_ms = max_over_ranks(sum(tg) / len(tg), world)
     int8_peak = 2.0 * bf16  # kind::i8 issues twice the bf16 rate on sm_100
     achieved = 2.0 * M * nl * K / (gemm_ms * 1e-3) / 1e12
@@ -348,11 +369,18 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
     ml = mxb.mx_linear.from_linear(lin.to(dev), mxb.int4d, 128)
     wbytes = ml._mx_weight._mx_packed.numel() + ml._mx_weight._mx_scales.numel() * 4
     g2 = torch.Generator().manual_seed(2)
-    for Mx in (1, 16, 128, 2048):
+    only = {"gemv1": (1,), "gemv16": (16,), "wo2048": (2048,)}.get(args.only)
+    for Mx in only or (1, 16, 128, 2048):
         x = torch.randn(Mx, 4096, generator=g2).bfloat16().to(dev)
         for _ in range(3):
             ml(x)
-        t = statistics.median(time_steps(lambda: ml(x), steps, flush, stream))
+        if only:  # profiling case: untimed launches
+            for _ in range(args.steps):
+                ml(x)
+            torch.cuda.synchronize()
+            return {"only": args.only}
+        fn = graphed(lambda: ml(x), stream)
+        t = statistics.median(time_steps(fn, steps, flush, stream))
         flops = 2.0 * Mx * 4096 * 11008
         byts = wbytes + x.numel() * 2 + Mx * 11008 * 4
         out[f"wonly_int4d_M{Mx}"] = {"ms": t, "tflops": flops / t / 1e9,
@@ -363,7 +391,8 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
         d = mxb.get_mx_dtype(dt)
         for _ in range(2):
             ops.quantize(x, d, 128)
-        t = statistics.median(time_steps(lambda: ops.quantize(x, d, 128), steps, flush, stream))
+        fn = graphed(lambda: ops.quantize(x, d, 128), stream)
+        t = statistics.median(time_steps(fn, steps, flush, stream))
         byts = n * 4 + n * d.bits / 8 + n / 128 * 4
         out[f"quantize_{dt}_fp32_2^{n.bit_length() - 1}"] = {
             "ms": t, "gbs": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / hbm}
@@ -378,7 +407,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true")
-    ap.add_argument("--only", default=None, choices=["gemm"],
+    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048"],
                     help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
