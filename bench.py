@@ -100,12 +100,14 @@ def graphed(fn, stream):
     """Capture fn (already warmed up) into a CUDA graph; returns a replay
     callable, or fn itself if capture is not possible."""
     g = torch.cuda.CUDAGraph()
+    torch.cuda.synchronize()
     try:
-        with torch.cuda.graph(g, stream=stream):
+        with torch.cuda.graph(g):  # captured on torch's side stream
             fn()
     except Exception:  # noqa: BLE001 - fall back to eager launches
         torch.cuda.synchronize()
         return fn
+    torch.cuda.synchronize()
     return g.replay
 
 

@@ -86,6 +86,130 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const XT* __restrict__ x
   }
 }
 
+// ── wide-load kernel for int4 / int8 codes ───────────────────────────────────
+// KW warps share one column range and split the CTA's K slice; each lane
+// loads LB bytes of codes per row (CPT columns), 8 rows ahead.  A code
+// becomes an exact float with one byte permute: the offset-binary code u
+// (two's complement with its sign bit flipped) placed under exponent byte
+// 0x4B reads as 2^23 + u.  x * s is formed once per row and multiplied by
+// the code, i.e. sum_k fl(x*s) * code instead of sum_k x * fl(code*s): the
+// two differ by one fp32 rounding per term.  Warp partials are added in a
+// fixed order in shared memory, so results are deterministic.
+constexpr int kWideWarps = 8;
+constexpr int kBatch = 8;
+
+template <int BITS, int LB>
+__device__ __forceinline__ void load_wide(const uint8_t* p, uint32_t (&w)[LB / 4]) {
+  if constexpr (LB == 16) {
+    uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (LB == 8) {
+    uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = __ldcs(reinterpret_cast<const uint32_t*>(p));
+  }
+}
+
+// 32 bits of codes -> 32/BITS exact floats, column order.
+template <int BITS>
+__device__ __forceinline__ void decode_word(uint32_t w, float* out) {
+  if constexpr (BITS == 4) {
+    const uint32_t v = w ^ 0x88888888u;  // two's complement -> offset binary (code + 8)
+    const uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      out[2 * k] = __fsub_rn(__int_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + k)), 8388616.0f);
+      out[2 * k + 1] =
+          __fsub_rn(__int_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + k)), 8388616.0f);
+    }
+  } else {  // BITS == 8
+    const uint32_t v = w ^ 0x80808080u;  // code + 128
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      out[k] = __fsub_rn(__int_as_float(__byte_perm(v, 0x4B000000u, 0x7440 + k)), 8388736.0f);
+  }
+}
+
+template <int BITS, int LB, int MT, typename XT>
+__global__ void __launch_bounds__(kWideWarps * 32) gemv_wide_kernel(
+    const XT* __restrict__ x, int M, int K, const uint8_t* __restrict__ W,
+    const float* __restrict__ ws, int N, int block, int krows, float* __restrict__ part) {
+  constexpr int CPT = LB * 8 / BITS;
+  constexpr int kCols = 32 * CPT;  // columns of one CTA
+  extern __shared__ __align__(16) float sm[];
+  float* xs = sm;                    // [MT][krows]
+  float* red = sm + MT * krows;      // [kWideWarps][MT][kCols]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k0 = blockIdx.y * krows;
+  const int kn = min(krows, K - k0);
+  for (int i = threadIdx.x; i < MT * krows; i += blockDim.x) {
+    const int m = i / krows, kk = i % krows;
+    xs[i] = (m < M && kk < kn) ? load_as_f32(x, (int64_t)m * K + k0 + kk) : 0.0f;
+  }
+  __syncthreads();
+
+  const int c0 = blockIdx.x * kCols + lane * CPT;
+  float acc[MT][CPT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) acc[m][c] = 0.0f;
+
+  if (c0 < N) {
+    const int64_t row_bytes = (int64_t)N * BITS / 8;
+    const int64_t nsb = N / block;
+    const int per_warp = (kn + kWideWarps - 1) / kWideWarps;
+    const int r0 = warp * per_warp, r1 = min(kn, r0 + per_warp);
+    const uint8_t* wp = W + (int64_t)k0 * row_bytes + (int64_t)c0 * BITS / 8;
+    const float* sp = ws + (int64_t)k0 * nsb + c0 / block;
+    for (int rb = r0; rb < r1; rb += kBatch) {
+      uint32_t words[kBatch][LB / 4];
+      float sc[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        if (rb + b < r1) {
+          load_wide<BITS, LB>(wp + (int64_t)(rb + b) * row_bytes, words[b]);
+          sc[b] = __ldg(sp + (int64_t)(rb + b) * nsb);
+        } else {
+#pragma unroll
+          for (int q = 0; q < LB / 4; ++q) words[b][q] = (BITS == 4) ? 0x88888888u : 0x80808080u;
+          sc[b] = 0.0f;  // code 0 and scale 0: adds nothing
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        float code[CPT];
+#pragma unroll
+        for (int q = 0; q < LB / 4; ++q) decode_word<BITS>(words[b][q], code + q * (32 / BITS));
+        const int kk = min(rb + b, kn - 1);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          const float xsv = __fmul_rn(xs[m * krows + kk], sc[b]);
+#pragma unroll
+          for (int c = 0; c < CPT; ++c) acc[m][c] = fmaf(xsv, code[c], acc[m][c]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int c = 0; c < CPT; c += 4)
+      *reinterpret_cast<float4*>(red + (warp * MT + m) * kCols + lane * CPT + c) =
+          make_float4(acc[m][c], acc[m][c + 1], acc[m][c + 2], acc[m][c + 3]);
+  __syncthreads();
+  for (int i = threadIdx.x; i < MT * kCols; i += blockDim.x) {
+    const int m = i / kCols, c = i % kCols;
+    const int col = blockIdx.x * kCols + c;
+    if (m >= M || col >= N) continue;
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWideWarps; ++w) s = __fadd_rn(s, red[(w * MT + m) * kCols + c]);
+    part[((int64_t)blockIdx.y * M + m) * N + col] = s;
+  }
+}
+
 __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ part,
                                                            int splits, int64_t mn,
                                                            float* __restrict__ y) {
@@ -125,6 +249,39 @@ int launch_t(int mt, dim3 grid, const XT* x, int M, int K, const uint8_t* W, con
   return MXB_E_DTYPE;
 }
 
+int wide_cpt(int bits, int lb) { return lb * 8 / bits; }
+
+size_t wide_smem(int mt, int krows, int cols) {
+  return (size_t)(mt * krows + kWideWarps * mt * cols) * sizeof(float);
+}
+
+template <int BITS, int LB, int MT, typename XT>
+int launch_wide_t(dim3 grid, const XT* x, int M, int K, const uint8_t* W, const float* ws, int N,
+                  int block, int krows, float* part, cudaStream_t st) {
+  auto kern = gemv_wide_kernel<BITS, LB, MT, XT>;
+  const size_t smem = wide_smem(MT, krows, 32 * LB * 8 / BITS);
+  if (smem > 48 * 1024)
+    MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<grid, kWideWarps * 32, smem, st>>>(x, M, K, W, ws, N, block, krows, part);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+template <int BITS, typename XT>
+int launch_wide(int mt, int lb, dim3 grid, const XT* x, int M, int K, const uint8_t* W,
+                const float* ws, int N, int block, int krows, float* part, cudaStream_t st) {
+  constexpr int LBN = BITS == 4 ? 4 : 8;  // 8 columns per thread for M > 2
+  if (lb == 16) {
+    if (mt == 1) return launch_wide_t<BITS, 16, 1, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
+    return launch_wide_t<BITS, 16, 2, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
+  }
+  switch (mt) {
+    case 4: return launch_wide_t<BITS, LBN, 4, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
+    case 8: return launch_wide_t<BITS, LBN, 8, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
+    default: return launch_wide_t<BITS, LBN, 16, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
+  }
+}
+
 }  // namespace
 
 namespace mxb {
@@ -135,7 +292,26 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
   if (M < 1 || M > 16 || K < 1 || N < kCols) return p;
   if (N % kCols || block % kCols || N % block) return p;
   if (((uintptr_t)w % (uintptr_t)bits) || ((uintptr_t)y % 16)) return p;
-  (void)kind;
+  const int mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16;
+  if (kind == MXB_KIND_INT && (bits == 4 || bits == 8)) {
+    const int lb = mt <= 2 ? 16 : (bits == 4 ? 4 : 8);
+    const int cpt = wide_cpt(bits, lb);
+    const int cols = 32 * cpt;
+    if (N % cpt == 0 && block % cpt == 0 && ((uintptr_t)w % lb) == 0) {
+      const int64_t groups = cdiv(N, cols);
+      int64_t splits = cdiv(3 * kSMs, groups);
+      int64_t krows = cdiv(cdiv(K, splits), 64) * 64;  // >= 8 rows per warp
+      if (krows > 1024) krows = 1024;
+      splits = cdiv(K, krows);
+      p.ok = true;
+      p.kernel = 1;
+      p.lb = lb;
+      p.splits = (int)splits;
+      p.krows = (int)krows;
+      p.ws_bytes = (size_t)splits * M * N * sizeof(float);
+      return p;
+    }
+  }
   const int64_t groups = cdiv(N, kCtaCols);
   int64_t splits = cdiv(4 * kSMs, groups);
   int64_t krows = cdiv(cdiv(K, splits), 8) * 8;
@@ -156,7 +332,24 @@ int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_
   dim3 grid((unsigned)cdiv(N, kCtaCols), (unsigned)plan.splits);
   const uint8_t* W = static_cast<const uint8_t*>(w);
   int rc;
-  if (x_dtype == MXB_F32)
+  if (plan.kernel == 1) {
+    dim3 g2((unsigned)cdiv(N, 32 * wide_cpt(bits, plan.lb)), (unsigned)plan.splits);
+    if (x_dtype == MXB_F32) {
+      const float* xf = static_cast<const float*>(x);
+      rc = bits == 4 ? launch_wide<4>(mt, plan.lb, g2, xf, (int)M, (int)K, W, ws, (int)N, block,
+                                      plan.krows, partial, st)
+                     : launch_wide<8>(mt, plan.lb, g2, xf, (int)M, (int)K, W, ws, (int)N, block,
+                                      plan.krows, partial, st);
+    } else if (x_dtype == MXB_BF16) {
+      const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+      rc = bits == 4 ? launch_wide<4>(mt, plan.lb, g2, xb, (int)M, (int)K, W, ws, (int)N, block,
+                                      plan.krows, partial, st)
+                     : launch_wide<8>(mt, plan.lb, g2, xb, (int)M, (int)K, W, ws, (int)N, block,
+                                      plan.krows, partial, st);
+    } else {
+      return MXB_E_DTYPE;
+    }
+  } else if (x_dtype == MXB_F32)
     rc = launch_t(mt, grid, static_cast<const float*>(x), (int)M, (int)K, W, ws, (int)N, bits,
                   kind, block, plan.krows, partial, st);
   else if (x_dtype == MXB_BF16)

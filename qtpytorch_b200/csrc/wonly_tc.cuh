@@ -14,10 +14,12 @@
 //   warp 0     TMA producer: x [256 x 64] bf16 (128-byte swizzle) and the
 //              packed codes [64 K rows x 128 N] per K step, 3-stage ring;
 //   warp 1     TMEM allocation and MMA issue (4 K=16 steps x 2 halves x planes);
-//   warps 2-5  transform: each thread dequantizes an 8 (N) x 8 (K) unit of
-//              codes and writes the bf16 planes straight into the 128-byte
-//              swizzled K-major layout (two plane buffers); then the epilogue
-//              (tcgen05.ld -> fp32 y).
+//   warps 2-9  transform, two groups of 4 taking alternate K steps (group j
+//              fills plane buffer j): each thread dequantizes an 8 (N) x 8 (K)
+//              unit of codes and writes the bf16 planes straight into the
+//              128-byte swizzled K-major layout; scales are fetched one step
+//              ahead.  Then the epilogue (tcgen05.ld -> fp32 y), group j
+//              draining accumulator j.
 // Included by gemm_tc.cu (shares its device error word).
 #pragma once
 
@@ -26,7 +28,8 @@ namespace wo {
 
 constexpr int BM = 256, BN = 128, BK = 64;  // BK in bf16 elements (128 bytes)
 constexpr int STAGES = 3;
-constexpr int kTransWarps = 4;
+constexpr int kTransWarps = 8;               // two groups of 4
+constexpr int kGroupWarps = kTransWarps / 2;
 constexpr int kThreads = 64 + 32 * kTransWarps;
 constexpr int kAHalf = 128 * BK * 2;      // 16 KB
 constexpr int kAStage = 2 * kAHalf;       // 32 KB
@@ -106,10 +109,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], 1 + kTransWarps);
+      mbar_init(&bars->empty[s], 1 + kGroupWarps);
     }
     for (int j = 0; j < 2; ++j) {
-      mbar_init(&bars->bready[j], kTransWarps);
+      mbar_init(&bars->bready[j], kGroupWarps);
       mbar_init(&bars->bfree[j], 1);
     }
     mbar_init(&bars->accfull, 1);
@@ -167,18 +170,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&bars->accfull);
     }
   } else {
-    // ── transform: one 8 (N) x 8 (K) unit per thread per K step ──
-    const int t = threadIdx.x - 64;
+    // ── transform: two groups of 4 warps take alternate K steps, group j
+    // filling plane buffer j; one 8 (N) x 8 (K) unit per thread per step ──
+    const int grp = (warp - 2) >> 2;
+    const int t = (threadIdx.x - 64) & 127;
     const int n8 = t & 15, k8 = t >> 4;  // n-group (16 of 8 columns), k-group (8 of 8 rows)
     const int nsb = N / block;
-    const float* sp = ws + (size_t)(n0 + n8 * 8) / block;
-    for (int ks = 0; ks < ksteps; ++ks) {
-      const int s = ks % STAGES, round = ks / STAGES;
-      const int j = ks & 1, usej = ks >> 1;
-      float sc[8];
-      const int kbase = ks * BK + k8 * 8;
+    const float* sp = ws + (size_t)(n0 + n8 * 8) / block + (size_t)(k8 * 8) * nsb;
+    float sc_next[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sc[i] = __ldg(sp + (size_t)(kbase + i) * nsb);
+    for (int i = 0; i < 8; ++i)
+      sc_next[i] = grp < ksteps ? __ldg(sp + (size_t)(grp * BK + i) * nsb) : 0.0f;
+    for (int ks = grp; ks < ksteps; ks += 2) {
+      const int s = ks % STAGES, round = ks / STAGES;
+      const int j = grp, usej = ks >> 1;
+      float sc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sc[i] = sc_next[i];
+      if (ks + 2 < ksteps) {  // scales of this group's next step, one step ahead
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sc_next[i] = __ldg(sp + (size_t)((ks + 2) * BK + i) * nsb);
+      }
       if (!mbar_wait_warp(&bars->full[s], round & 1, kErrTimeoutFull)) break;
       uint64_t word[8];
       const uint8_t* cp = sC + s * kCodeStageMax + (k8 * 8) * kCodeRow + n8 * BITS;
@@ -219,8 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (mbar_wait_warp(&bars->accfull, 0, kErrTimeoutDone)) {
       tc_fence_after();
       const int q = warp & 3;
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
+      {
+        const int h = grp;  // accumulator (M half) of this warp's group
         const int m = m0 + h * 128 + q * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
