@@ -255,7 +255,7 @@ def run_ours(args, world, rank, local):
         rc = lib.mxb_qgemm(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales), qa._mx_scales.numel(),
                            L.ptr(w.codes), L.ptr(w.scales), w.scales.numel(), M, K, nl, 8,
                            BLOCK, 32, L.ptr(cp), L.ptr(cs), L.ptr(c32), L.ptr(ws), wsb,
-                           stream.cuda_stream)
+                           torch.cuda.current_stream(dev).cuda_stream)
         L.check(rc, "mxb_qgemm")
 
     for _ in range(max(args.warmup, 3)):
