@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const XT* __restrict__ x
 // two differ by one fp32 rounding per term.  Warp partials are added in a
 // fixed order in shared memory, so results are deterministic.
 constexpr int kWideWarps = 8;
-constexpr int kBatch = 8;
+constexpr int kBatch = 4;  // rows per load batch (two batches in flight)
 
 template <int BITS, int LB>
 __device__ __forceinline__ void load_wide(const uint8_t* p, uint32_t (&w)[LB / 4]) {
@@ -111,23 +111,26 @@ __device__ __forceinline__ void load_wide(const uint8_t* p, uint32_t (&w)[LB / 4
   }
 }
 
-// 32 bits of codes -> 32/BITS exact floats, column order.
+// 32 bits of codes -> 16/BITS exact float pairs (columns 2p, 2p+1).
 template <int BITS>
-__device__ __forceinline__ void decode_word(uint32_t w, float* out) {
+__device__ __forceinline__ void decode_word2(uint32_t w, uint64_t* out) {
   if constexpr (BITS == 4) {
     const uint32_t v = w ^ 0x88888888u;  // two's complement -> offset binary (code + 8)
     const uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      out[2 * k] = __fsub_rn(__int_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + k)), 8388616.0f);
-      out[2 * k + 1] =
-          __fsub_rn(__int_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + k)), 8388616.0f);
-    }
-  } else {  // BITS == 8
-    const uint32_t v = w ^ 0x80808080u;  // code + 128
+    const uint64_t bias = pack2(8388616.0f, 8388616.0f);  // 2^23 + 8
 #pragma unroll
     for (int k = 0; k < 4; ++k)
-      out[k] = __fsub_rn(__int_as_float(__byte_perm(v, 0x4B000000u, 0x7440 + k)), 8388736.0f);
+      out[k] = fsub2(pack2(__int_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + k)),
+                           __int_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + k))),
+                     bias);
+  } else {  // BITS == 8
+    const uint32_t v = w ^ 0x80808080u;  // code + 128
+    const uint64_t bias = pack2(8388736.0f, 8388736.0f);  // 2^23 + 128
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      out[k] = fsub2(pack2(__int_as_float(__byte_perm(v, 0x4B000000u, 0x7440 + 2 * k)),
+                           __int_as_float(__byte_perm(v, 0x4B000000u, 0x7441 + 2 * k))),
+                     bias);
   }
 }
 
@@ -150,11 +153,11 @@ __global__ void __launch_bounds__(kWideWarps * 32) gemv_wide_kernel(
   __syncthreads();
 
   const int c0 = blockIdx.x * kCols + lane * CPT;
-  float acc[MT][CPT];
+  uint64_t acc[MT][CPT / 2];  // packed pairs of columns
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) acc[m][c] = 0.0f;
+    for (int c = 0; c < CPT / 2; ++c) acc[m][c] = 0ull;
 
   if (c0 < N) {
     const int64_t row_bytes = (int64_t)N * BITS / 8;
@@ -163,41 +166,56 @@ __global__ void __launch_bounds__(kWideWarps * 32) gemv_wide_kernel(
     const int r0 = warp * per_warp, r1 = min(kn, r0 + per_warp);
     const uint8_t* wp = W + (int64_t)k0 * row_bytes + (int64_t)c0 * BITS / 8;
     const float* sp = ws + (int64_t)k0 * nsb + c0 / block;
-    for (int rb = r0; rb < r1; rb += kBatch) {
-      uint32_t words[kBatch][LB / 4];
-      float sc[kBatch];
+    // Two register buffers of kBatch rows: the loads of batch i+1 are in
+    // flight while batch i is computed.
+    uint32_t wa[kBatch][LB / 4], wb[kBatch][LB / 4];
+    float sa_[kBatch], sb_[kBatch];
+    auto load = [&](int rb, uint32_t (&wd)[kBatch][LB / 4], float (&sc)[kBatch]) {
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) {
         if (rb + b < r1) {
-          load_wide<BITS, LB>(wp + (int64_t)(rb + b) * row_bytes, words[b]);
+          load_wide<BITS, LB>(wp + (int64_t)(rb + b) * row_bytes, wd[b]);
           sc[b] = __ldg(sp + (int64_t)(rb + b) * nsb);
         } else {
 #pragma unroll
-          for (int q = 0; q < LB / 4; ++q) words[b][q] = (BITS == 4) ? 0x88888888u : 0x80808080u;
+          for (int q = 0; q < LB / 4; ++q) wd[b][q] = (BITS == 4) ? 0x88888888u : 0x80808080u;
           sc[b] = 0.0f;  // code 0 and scale 0: adds nothing
         }
       }
+    };
+    auto compute = [&](int rb, const uint32_t (&wd)[kBatch][LB / 4], const float (&sc)[kBatch]) {
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) {
-        float code[CPT];
+        uint64_t code[CPT / 2];
 #pragma unroll
-        for (int q = 0; q < LB / 4; ++q) decode_word<BITS>(words[b][q], code + q * (32 / BITS));
+        for (int q = 0; q < LB / 4; ++q) decode_word2<BITS>(wd[b][q], code + q * (16 / BITS));
         const int kk = min(rb + b, kn - 1);
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
           const float xsv = __fmul_rn(xs[m * krows + kk], sc[b]);
+          const uint64_t xs2 = pack2(xsv, xsv);
 #pragma unroll
-          for (int c = 0; c < CPT; ++c) acc[m][c] = fmaf(xsv, code[c], acc[m][c]);
+          for (int c = 0; c < CPT / 2; ++c) acc[m][c] = ffma2(xs2, code[c], acc[m][c]);
         }
       }
+    };
+    if (r0 < r1) load(r0, wa, sa_);
+    for (int rb = r0; rb < r1; rb += 2 * kBatch) {
+      if (rb + kBatch < r1) load(rb + kBatch, wb, sb_);
+      compute(rb, wa, sa_);
+      if (rb + kBatch >= r1) break;
+      if (rb + 2 * kBatch < r1) load(rb + 2 * kBatch, wa, sa_);
+      compute(rb + kBatch, wb, sb_);
     }
   }
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int c = 0; c < CPT; c += 4)
-      *reinterpret_cast<float4*>(red + (warp * MT + m) * kCols + lane * CPT + c) =
-          make_float4(acc[m][c], acc[m][c + 1], acc[m][c + 2], acc[m][c + 3]);
+    for (int c = 0; c < CPT / 2; c += 2) {
+      const float2 lo = unpack2(acc[m][c]), hi = unpack2(acc[m][c + 1]);
+      *reinterpret_cast<float4*>(red + (warp * MT + m) * kCols + lane * CPT + 2 * c) =
+          make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
   __syncthreads();
   for (int i = threadIdx.x; i < MT * kCols; i += blockDim.x) {
     const int m = i / kCols, c = i % kCols;

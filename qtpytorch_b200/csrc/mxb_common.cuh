@@ -89,6 +89,36 @@ __device__ __forceinline__ float dequant_code(uint32_t raw, float scale) {
   }
 }
 
+// ── packed fp32 pairs (add/sub/mul/fma .f32x2, sm_100a): each lane is
+// rounded exactly as the scalar .rn instruction would round it.  ptxas may
+// fuse a packed mul followed by a packed add, so code that must round the
+// product separately keeps its add scalar.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 __device__ __forceinline__ float load_as_f32(const float* p, int64_t i) { return __ldg(p + i); }
 __device__ __forceinline__ float load_as_f32(const __nv_bfloat16* p, int64_t i) {
   return __bfloat162float(p[i]);

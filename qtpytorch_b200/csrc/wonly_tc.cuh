@@ -177,19 +177,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n8 = t & 15, k8 = t >> 4;  // n-group (16 of 8 columns), k-group (8 of 8 rows)
     const int nsb = N / block;
     const float* sp = ws + (size_t)(n0 + n8 * 8) / block + (size_t)(k8 * 8) * nsb;
-    float sc_next[8];
+    // When the tile's 128 columns share one scale block (block % 128 == 0)
+    // the warp needs only 16 scales per step (its two 8-row K groups): lane
+    // l loads row l % 16 and the others read it by shuffle.  Otherwise each
+    // thread loads its own 8.  Either way one step ahead.
+    const bool one_block = block % BN == 0;
+    const int wrow0 = ((t >> 5) << 4);  // first K row of this warp within a step
+    const float* sp1 = ws + (size_t)n0 / block + (size_t)(wrow0 + (lane & 15)) * nsb;
+    float sc_next[8], s1_next = 0.0f;
+    if (grp < ksteps) {
+      if (one_block) {
+        s1_next = __ldg(sp1 + (size_t)(grp * BK) * nsb);
+      } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      sc_next[i] = grp < ksteps ? __ldg(sp + (size_t)(grp * BK + i) * nsb) : 0.0f;
+        for (int i = 0; i < 8; ++i) sc_next[i] = __ldg(sp + (size_t)(grp * BK + i) * nsb);
+      }
+    }
     for (int ks = grp; ks < ksteps; ks += 2) {
       const int s = ks % STAGES, round = ks / STAGES;
       const int j = grp, usej = ks >> 1;
       float sc[8];
+      if (one_block) {
+        const float s1 = s1_next;
+        if (ks + 2 < ksteps) s1_next = __ldg(sp1 + (size_t)((ks + 2) * BK) * nsb);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sc[i] = sc_next[i];
-      if (ks + 2 < ksteps) {  // scales of this group's next step, one step ahead
+        for (int i = 0; i < 8; ++i) sc[i] = __shfl_sync(0xffffffffu, s1, ((lane >> 4) << 3) + i);
+      } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sc_next[i] = __ldg(sp + (size_t)((ks + 2) * BK + i) * nsb);
+        for (int i = 0; i < 8; ++i) sc[i] = sc_next[i];
+        if (ks + 2 < ksteps) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sc_next[i] = __ldg(sp + (size_t)((ks + 2) * BK + i) * nsb);
+        }
       }
       if (!mbar_wait_warp(&bars->full[s], round & 1, kErrTimeoutFull)) break;
       uint64_t word[8];
