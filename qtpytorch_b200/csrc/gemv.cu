@@ -316,9 +316,11 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
     const int cpt = wide_cpt(bits, lb);
     const int cols = 32 * cpt;
     if (N % cpt == 0 && block % cpt == 0 && ((uintptr_t)w % lb) == 0) {
+      // one wave: about two resident CTAs per SM, K rows a multiple of 32
       const int64_t groups = cdiv(N, cols);
-      int64_t splits = cdiv(3 * kSMs, groups);
-      int64_t krows = cdiv(cdiv(K, splits), 64) * 64;  // >= 8 rows per warp
+      int64_t splits = (2 * kSMs) / groups;
+      if (splits < 1) splits = 1;
+      int64_t krows = cdiv(cdiv(K, splits), 32) * 32;
       if (krows > 1024) krows = 1024;
       splits = cdiv(K, krows);
       p.ok = true;

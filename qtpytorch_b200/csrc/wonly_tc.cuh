@@ -223,11 +223,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* pmid = sP + (2 * j + 1) * kPlane;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const int r = n8 * 8 + c;  // N row of the plane
+        // rotate the column order by n8 so the lanes of a warp store to 8
+        // different 16-byte bank groups (r & 7 varies across lanes)
+        const int cc = (c + n8) & 7;
+        const int r = n8 * 8 + cc;  // N row of the plane
         float w[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          w[i] = wdeq<BITS, KIND>((uint32_t)(word[i] >> (c * BITS)) & ((1u << BITS) - 1u), sc[i]);
+          w[i] = wdeq<BITS, KIND>((uint32_t)(word[i] >> (cc * BITS)) & ((1u << BITS) - 1u), sc[i]);
         uint4 hv, mv;
         uint32_t* h4 = reinterpret_cast<uint32_t*>(&hv);
         uint32_t* m4 = reinterpret_cast<uint32_t*>(&mv);
