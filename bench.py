@@ -230,7 +230,7 @@ def run_ours(args, world, rank, local):
     def flush():
         flush_buf.zero_()
 
-    if args.only in ("gemv1", "gemv16", "wo2048"):
+    if args.only in ("gemv1", "gemv16", "wo2048", "quant"):
         print(json.dumps(run_extras(args, dev, flush, torch.cuda.current_stream(dev), hbm, bf16)))
         return
 
@@ -363,6 +363,12 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
     from qtpytorch_b200 import ops
     out = {}
     steps = max(3, min(args.steps, 10))
+    if args.only == "quant":  # profiling case: int4d quantize of 2^26 fp32 values
+        x = torch.randn(1 << 26, device=dev)
+        for _ in range(3 + args.steps):
+            ops.quantize(x, mxb.int4d, 128)
+        torch.cuda.synchronize()
+        return {"only": "quant"}
     g = torch.Generator().manual_seed(1)
     W = torch.randn(11008, 4096, generator=g) * 0.02
     lin = torch.nn.Linear(4096, 11008, bias=False)
@@ -388,6 +394,14 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
         out[f"wonly_int4d_M{Mx}"] = {"ms": t, "tflops": flops / t / 1e9,
                                      "gbs": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / hbm,
                                      "tensor_frac_bf16": flops / t / 1e9 / bf16}
+        if Mx >= 128:  # fast mode: weights rounded to bf16 once (one MMA per K step)
+            ml.mode = "fast"
+            ml(x)
+            fn = graphed(lambda: ml(x), stream)
+            t = statistics.median(time_steps(fn, steps, flush, stream))
+            ml.mode = "parity"
+            out[f"wonly_int4d_M{Mx}_fast"] = {"ms": t, "tflops": flops / t / 1e9,
+                                              "tensor_frac_bf16": flops / t / 1e9 / bf16}
     for dt, n in (("int2d", 1 << 28), ("int4d", 1 << 28), ("float4d", 1 << 26)):
         x = torch.randn(n, device=dev)
         d = mxb.get_mx_dtype(dt)
@@ -409,7 +423,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true")
-    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048"],
+    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant"],
                     help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

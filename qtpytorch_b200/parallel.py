@@ -82,15 +82,34 @@ def sharded_qgemm(qa: mx_tensor, w: ShardedQGemmWeight,
     widths = {b - a for a, b in w.shards}
     if len(widths) != 1:
         raise NotImplementedError("uneven column shards need a variable-size gather")
-    G = w.world
-    gp = torch.empty((G,) + tuple(c_packed.shape), dtype=c_packed.dtype, device=c_packed.device)
-    gs = torch.empty((G,) + tuple(c_scales.shape), dtype=c_scales.dtype, device=c_scales.device)
-    dist.all_gather_into_tensor(gp, c_packed, group=group)
-    dist.all_gather_into_tensor(gs, c_scales, group=group)
-    # [G, M, nl/2 words] -> [M, G, nl/2] (row-major C); scales likewise
-    words = gp.view(G, M, -1).transpose(0, 1).reshape(-1)
-    scales = gs.view(G, M, -1).transpose(0, 1).reshape(-1)
+    words, scales = gather_columns(c_packed, c_scales, M, w.world, group)
     return mx_tensor(words, scales, out_dt, torch.Size([M, w.N]), M * w.N, w.block)
+
+
+def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
+    """[world, *t.shape]: one all-gather (into one buffer on NCCL)."""
+    out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, t, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), t, group=group)
+    return out
+
+
+def gather_columns(c_packed: torch.Tensor, c_scales: torch.Tensor, M: int, world: int,
+                   group=None):
+    """Assemble row-major packed C from equal column shards.
+
+    Each rank holds C[:, n0:n1] packed row-major ([M, nl] codes as storage
+    words, [M, nl/block] scales).  Because every shard width is a whole
+    number of scale blocks, row m of C is the concatenation over ranks of
+    their row m: gather [G, M, ...] and reorder to [M, G, ...].
+    """
+    gp = _all_gather(c_packed.contiguous(), world, group)
+    gs = _all_gather(c_scales.contiguous(), world, group)
+    words = gp.view(world, M, -1).transpose(0, 1).reshape(-1)
+    scales = gs.view(world, M, -1).transpose(0, 1).reshape(-1)
+    return words, scales
 
 
 def sharded_quantize(x: torch.Tensor, dt, block: int, world: int, rank: int):
