@@ -160,6 +160,18 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
+def profiled_traffic(key):
+    """DRAM bytes per launch recorded from an ncu capture (profiles/traffic.txt)."""
+    p = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        f = line.split()
+        if len(f) == 2 and f[0] == key:
+            return int(f[1])
+    return None
+
+
 def make_inputs():
     torch.manual_seed(0)
     a = torch.randn(M, K)
@@ -286,10 +298,7 @@ def run_ours(args, world, rank, local):
     gemm_ms = max_over_ranks(sum(tg) / len(tg), world)
     int8_peak = 2.0 * bf16  # kind::i8 issues twice the bf16 rate on sm_100
     achieved = 2.0 * M * nl * K / (gemm_ms * 1e-3) / 1e12
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tf):
-        traffic = json.load(open(tf)).get("qgemm_int8_4096", None)
+    traffic = profiled_traffic("qgemm_int8_4096") if world == 1 else None
 
     # e2e: host fp32 operands -> public API -> host packed result
     a_pin = a_h.pin_memory()
