@@ -286,7 +286,8 @@ def run_ours(args, world, rank, local):
     n0 = lib.mxb_launch_count()
     step()
     launches = (lib.mxb_launch_count() - n0) * args.steps
-    step_g = graphed(step, stream)
+    # N > 1: eager steps (the NCCL gather is not graph-captured here)
+    step_g = graphed(step, stream) if world == 1 else step
     with Clocks(local) as clk:
         barrier(world)
         ts = time_steps(step_g, args.steps, flush, stream)
