@@ -34,13 +34,17 @@ constexpr int kSMs = 148;
 __host__ __device__ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // NaN-propagating max of |v| (torch.amax propagates NaN).
-__device__ __forceinline__ float amax_step(float acc, float v) {
-  float a = fabsf(v);
-  return (a > acc || a != a) ? a : acc;
-}
 __device__ __forceinline__ float nan_max(float a, float b) {
-  return (a > b || a != a) ? a : b;
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
+__device__ __forceinline__ float nan_min(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float amax_step(float acc, float v) { return nan_max(acc, fabsf(v)); }
 
 // Sorted float4 grid (16 entries, -0 before +0) and its 15 bucket
 // boundaries fl((g[i]+g[i+1])*0.5), as bit patterns.  Values are the

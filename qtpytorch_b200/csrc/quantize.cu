@@ -23,10 +23,6 @@ namespace {
 // Quantizer flavours.
 enum QMode { Q_INT_RECIP = 0, Q_INT_DIV = 1, Q_FLOAT4 = 2 };
 
-__device__ __forceinline__ float clamp_keep_nan(float v, float m) {
-  return v < -m ? -m : (v > m ? m : v);
-}
-
 // Per-block factor: returns scale (stored) and `mul` (what codes use).
 template <int BITS, int MODE>
 __device__ __forceinline__ void block_factor(float amax, float& scale, float& mul) {
@@ -55,9 +51,11 @@ __device__ __forceinline__ uint32_t code_of(float v, float mul) {
   } else {
     const float m = (float)((1 << (BITS - 1)) - 1);
     float q = (MODE == Q_INT_RECIP) ? __fmul_rn(v, mul) : __fdiv_rn(v, mul);
-    q = clamp_keep_nan(q, m);
-    int c = __float2int_rn(q);  // round half to even; NaN -> 0 after masking
-    return (uint32_t)c & ((1u << BITS) - 1u);
+    q = nan_min(nan_max(q, -m), m);  // clamp; NaN stays NaN
+    // Round half to even by adding 1.5 * 2^23 (|q| <= 32767 < 2^22): the sum's
+    // low mantissa bits are the two's-complement code.  NaN -> bits 0x7FC00000,
+    // whose low 16 bits are 0, the code the reference stores for NaN.
+    return __float_as_uint(__fadd_rn(q, 12582912.0f)) & ((1u << BITS) - 1u);
   }
 }
 
