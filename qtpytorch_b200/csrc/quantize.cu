@@ -53,9 +53,10 @@ __device__ __forceinline__ uint32_t code_of(float v, float mul) {
     float q = (MODE == Q_INT_RECIP) ? __fmul_rn(v, mul) : __fdiv_rn(v, mul);
     q = nan_min(nan_max(q, -m), m);  // clamp; NaN stays NaN
     // Round half to even by adding 1.5 * 2^23 (|q| <= 32767 < 2^22): the sum's
-    // low mantissa bits are the two's-complement code.  NaN -> bits 0x7FC00000,
-    // whose low 16 bits are 0, the code the reference stores for NaN.
-    return __float_as_uint(__fadd_rn(q, 12582912.0f)) & ((1u << BITS) - 1u);
+    // low mantissa bits are the two's-complement code.  NaN stores code 0, as
+    // the reference's NaN -> int conversion does.
+    const uint32_t c = __float_as_uint(__fadd_rn(q, 12582912.0f)) & ((1u << BITS) - 1u);
+    return q == q ? c : 0u;
   }
 }
 
