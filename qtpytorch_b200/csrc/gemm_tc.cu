@@ -384,9 +384,6 @@ extern "C" int mxb_device_error(int clear) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, mxb::g_mxb_device_error, sizeof(int)) != cudaSuccess)
     return MXB_E_CUDA;
-  const int g = mxb::gemv_device_error(clear);  // the GEMV's own word (its translation unit)
-  if (g < 0) return g;
-  if (v == 0 && g != 0) v = 6;
   if (clear && v != 0) {
     int z = 0;
     if (cudaMemcpyToSymbol(mxb::g_mxb_device_error, &z, sizeof(int)) != cudaSuccess)

@@ -267,25 +267,6 @@ int launch_t(int mt, dim3 grid, const XT* x, int M, int K, const uint8_t* W, con
   return MXB_E_DTYPE;
 }
 
-#include "gemv_bulk.cuh"
-
-template <int BITS, typename XT>
-int launch_bulk(int mt, dim3 grid, const XT* x, int M, int K, const uint8_t* W, const float* ws,
-                int N, int block, int krows, float* part, cudaStream_t st) {
-  const size_t smem = bulk_smem(mt, krows);
-  if (mt == 1) {
-    auto kern = gemv_bulk_kernel<BITS, 1, XT>;
-    MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<grid, kBulkThreads, smem, st>>>(x, M, K, W, ws, N, block, krows, part);
-  } else {
-    auto kern = gemv_bulk_kernel<BITS, 2, XT>;
-    MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<grid, kBulkThreads, smem, st>>>(x, M, K, W, ws, N, block, krows, part);
-  }
-  MXB_LAUNCH_CHECK();
-  return MXB_OK;
-}
-
 int wide_cpt(int bits, int lb) { return lb * 8 / bits; }
 
 size_t wide_smem(int mt, int krows, int cols) {
@@ -323,16 +304,6 @@ int launch_wide(int mt, int lb, dim3 grid, const XT* x, int M, int K, const uint
 
 namespace mxb {
 
-int gemv_device_error(int clear) {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_gemv_error, sizeof(int)) != cudaSuccess) return MXB_E_CUDA;
-  if (clear && v != 0) {
-    int z = 0;
-    if (cudaMemcpyToSymbol(g_gemv_error, &z, sizeof(int)) != cudaSuccess) return MXB_E_CUDA;
-  }
-  return v;
-}
-
 GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,
                    const void* w, const void* y) {
   GemvPlan p{false, 0, 0, 0};
@@ -353,8 +324,7 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
       if (krows > 1024) krows = 1024;
       splits = cdiv(K, krows);
       p.ok = true;
-      // M <= 2 with 16-byte aligned rows: the bulk-copy-staged kernel
-      p.kernel = (mt <= 2 && ((uintptr_t)w % 16) == 0) ? 2 : 1;
+      p.kernel = 1;
       p.lb = lb;
       p.splits = (int)splits;
       p.krows = (int)krows;
@@ -382,24 +352,7 @@ int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_
   dim3 grid((unsigned)cdiv(N, kCtaCols), (unsigned)plan.splits);
   const uint8_t* W = static_cast<const uint8_t*>(w);
   int rc;
-  if (plan.kernel == 2) {
-    dim3 g2((unsigned)cdiv(N, 32 * (128 / bits)), (unsigned)plan.splits);
-    if (x_dtype == MXB_F32) {
-      const float* xf = static_cast<const float*>(x);
-      rc = bits == 4 ? launch_bulk<4>(mt, g2, xf, (int)M, (int)K, W, ws, (int)N, block,
-                                      plan.krows, partial, st)
-                     : launch_bulk<8>(mt, g2, xf, (int)M, (int)K, W, ws, (int)N, block,
-                                      plan.krows, partial, st);
-    } else if (x_dtype == MXB_BF16) {
-      const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
-      rc = bits == 4 ? launch_bulk<4>(mt, g2, xb, (int)M, (int)K, W, ws, (int)N, block,
-                                      plan.krows, partial, st)
-                     : launch_bulk<8>(mt, g2, xb, (int)M, (int)K, W, ws, (int)N, block,
-                                      plan.krows, partial, st);
-    } else {
-      return MXB_E_DTYPE;
-    }
-  } else if (plan.kernel == 1) {
+  if (plan.kernel == 1) {
     dim3 g2((unsigned)cdiv(N, 32 * wide_cpt(bits, plan.lb)), (unsigned)plan.splits);
     if (x_dtype == MXB_F32) {
       const float* xf = static_cast<const float*>(x);

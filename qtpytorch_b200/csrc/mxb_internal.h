@@ -31,7 +31,6 @@ struct GemvPlan {
 };
 GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,
                    const void* w, const void* y);
-int gemv_device_error(int clear);  // nonzero if a GEMV wait gave up; MXB_E_CUDA on failure
 int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_t K,
              const void* w, const float* ws, int64_t N, int bits, int kind, int block,
              float* y, float* partial, cudaStream_t st);
