@@ -14,7 +14,7 @@ namespace mxb {
 // `__device__ int g_mxb_device_error` (0 = ok) before including this header;
 // mxb_device_error() reads and clears it.
 
-constexpr uint32_t kSpinLimit = 1u << 21;  // polls of at most ~1 us each: ~2 s bound
+constexpr uint32_t kSpinLimit = 1u << 24;
 
 enum DeviceError : int {
   kErrTimeoutFull = 1,
@@ -50,16 +50,14 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
       : "memory");
 }
 
-// One poll; the suspend-time hint lets the hardware park the thread (up to
-// ~1 us) until the phase completes instead of spinning on issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+      : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
