@@ -43,8 +43,11 @@ int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
   const bool sb_ok = b_nscales == kbn * N;
   char* ws = static_cast<char*>(workspace);
   size_t left = workspace ? workspace_bytes : 0;
+  const bool tc = tc_qgemm_eligible(M, K, N, bits, block, sa_ok, sb_ok, a_packed, b_packed, c_f32);
+  // int16d output: the tcgen05 kernel requantizes in its epilogue
+  const bool fused = tc && out_bits == 16 && ((uintptr_t)c_packed % 16) == 0;
   float* C = c_f32;
-  if (C == nullptr) {
+  if (C == nullptr && !fused) {
     const size_t need = align_up((size_t)M * N * sizeof(float));
     if (left < need) return MXB_E_WORKSPACE;
     C = reinterpret_cast<float*>(ws);
@@ -52,17 +55,19 @@ int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
     left -= need;
   }
   int rc;
-  if (tc_qgemm_eligible(M, K, N, bits, block, sa_ok, sb_ok, a_packed, b_packed, C)) {
+  if (tc) {
     const size_t need = align_up(tc_qgemm_workspace(M, K, N, bits));
     if (left < need) return MXB_E_WORKSPACE;
-    rc = tc_qgemm(a_packed, a_scales, b_packed, b_scales, M, K, N, bits, block, C, ws, need, st);
+    rc = tc_qgemm(a_packed, a_scales, b_packed, b_scales, M, K, N, bits, block, C,
+                  fused ? static_cast<uint32_t*>(c_packed) : nullptr, fused ? c_scales : nullptr,
+                  ws, need, st);
     ws += need;
     left -= need;
   } else {
     rc = qgemm_generic(a_packed, a_scales, sa_ok, b_packed, b_scales, sb_ok, M, K, N, bits,
                        block, C, st);
   }
-  if (rc != MXB_OK || out_bits == 32) return rc;
+  if (rc != MXB_OK || out_bits == 32 || fused) return rc;
   return mxb_requant_f32(C, M * N, block, out_bits, c_packed, c_scales, left ? ws : nullptr,
                          left, st);
 }

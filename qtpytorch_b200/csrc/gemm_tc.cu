@@ -42,7 +42,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kTileA = BM * BKB;   // 16 KB
 constexpr int kTileB = BN * BKB;   // 16 KB
 constexpr int kTmemCols = 2 * BN;  // two int32 accumulators
-constexpr size_t kBarsBytes = 4096 + 512;  // >= sizeof(Bars), checked below
+constexpr size_t kBarsBytes = 8192;  // >= sizeof(Bars), checked below
 constexpr size_t kSmemBytes = 1024 + (size_t)STAGES * (kTileA + kTileB) + kBarsBytes;
 
 struct Bars {
@@ -54,6 +54,8 @@ struct Bars {
   uint32_t tmem_base;
   // per-warp double buffer of B scales, read back as float4 broadcasts
   alignas(16) float sbw[kEpiWarps][2 * kEpiCols];
+  // per-row absmax of each 32-column slice, for the fused requantization
+  float slice_amax[BN / kEpiCols][BM];
 };
 static_assert(sizeof(Bars) <= kBarsBytes, "barrier block overflows its shared-memory slot");
 static_assert(offsetof(Bars, sbw) % 16 == 0, "float4 reads of sbw need 16-byte alignment");
@@ -61,7 +63,8 @@ static_assert(offsetof(Bars, sbw) % 16 == 0, "float4 reads of sbw need 16-byte a
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const float* __restrict__ sa,
-                    const float* __restrict__ sb, int M, int N, int K, float* __restrict__ C) {
+                    const float* __restrict__ sb, int M, int N, int K, float* __restrict__ C,
+                    uint32_t* __restrict__ q_words, float* __restrict__ q_scales) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -188,11 +191,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    float4* out = reinterpret_cast<float4*>(C + (size_t)m * N + n0 + col0);
+    if (C != nullptr) {
+      float4* out = reinterpret_cast<float4*>(C + (size_t)m * N + n0 + col0);
 #pragma unroll
-    for (int c4 = 0; c4 < kEpiCols / 4; ++c4) {
-      const float2 lo = unpack2(acc[2 * c4]), hi = unpack2(acc[2 * c4 + 1]);
-      out[c4] = make_float4(lo.x, lo.y, hi.x, hi.y);
+      for (int c4 = 0; c4 < kEpiCols / 4; ++c4) {
+        const float2 lo = unpack2(acc[2 * c4]), hi = unpack2(acc[2 * c4 + 1]);
+        out[c4] = make_float4(lo.x, lo.y, hi.x, hi.y);
+      }
+    }
+    if (q_words != nullptr) {
+      // Fused int16d requantization (mxtorch.py:1371-1378): the 128 columns
+      // of this tile row are one scale block (N % 128 == 0, block 128).
+      float a = 0.0f;
+#pragma unroll
+      for (int c = 0; c < kEpiCols / 2; ++c) {
+        const float2 v = unpack2(acc[c]);
+        a = amax_step(amax_step(a, v.x), v.y);
+      }
+      bars->slice_amax[ew >> 2][row] = a;
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");  // promotion warps only
+#pragma unroll
+      for (int s = 0; s < BN / kEpiCols; ++s) a = nan_max(a, bars->slice_amax[s][row]);
+      const float cs = __fdiv_rn(a < 1e-12f ? 1e-12f : a, 32767.0f);
+      uint32_t w[kEpiCols / 2];
+#pragma unroll
+      for (int c = 0; c < kEpiCols / 2; ++c) {
+        const float2 v = unpack2(acc[c]);
+        uint32_t code[2];
+        const float vv[2] = {v.x, v.y};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float qv = nan_min(nan_max(__fdiv_rn(vv[h], cs), -32767.0f), 32767.0f);
+          // round half to even by adding 1.5 * 2^23; NaN stores code 0
+          const uint32_t bits = __float_as_uint(__fadd_rn(qv, 12582912.0f)) & 0xFFFFu;
+          code[h] = qv == qv ? bits : 0u;
+        }
+        w[c] = code[0] | (code[1] << 16);
+      }
+      uint4* qo = reinterpret_cast<uint4*>(q_words + ((size_t)m * N + n0 + col0) / 2);
+#pragma unroll
+      for (int c = 0; c < kEpiCols / 8; ++c) qo[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+      if (ew < 4) q_scales[((size_t)m * N + n0) / BN] = cs;
     }
   }
   __syncthreads();
@@ -297,7 +336,8 @@ size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits) {
 }
 
 int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
-             int64_t K, int64_t N, int bits, int block, float* C, void* ws, size_t wsb,
+             int64_t K, int64_t N, int bits, int block, float* C, uint32_t* q_words,
+             float* q_scales, void* ws, size_t wsb,
              cudaStream_t st) {
   (void)block;
   const void* a8 = a;
@@ -320,7 +360,8 @@ int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int
   MXB_CUDA_TRY(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
   dim3 grid((unsigned)(N / BN), (unsigned)(M / BM));
-  qgemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C);
+  qgemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C,
+                                                      q_words, q_scales);
   MXB_LAUNCH_CHECK();
   return MXB_OK;
 }

@@ -41,7 +41,8 @@ bool tc_qgemm_eligible(int64_t M, int64_t K, int64_t N, int bits, int block, boo
                        bool sb_ok, const void* a, const void* b, const float* c);
 size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits);
 int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
-             int64_t K, int64_t N, int bits, int block, float* C, void* ws, size_t wsb,
+             int64_t K, int64_t N, int bits, int block, float* C, uint32_t* q_words,
+             float* q_scales, void* ws, size_t wsb,
              cudaStream_t st);
 bool tc_wonly_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
                        int64_t N, int bits, int kind, int block, const float* y);
