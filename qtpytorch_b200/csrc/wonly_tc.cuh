@@ -14,11 +14,12 @@
 //   warp 0     TMA producer: x [256 x 64] bf16 (128-byte swizzle) and the
 //              packed codes [64 K rows x 128 N] per K step, 3-stage ring;
 //   warp 1     TMEM allocation and MMA issue (4 K=16 steps x 2 halves x planes);
-//   warps 2-17 transform, all on every K step (two plane buffers alternate
-//              between steps): each thread dequantizes 2 columns x 8 K of an
-//              8 (N) x 8 (K) unit of codes and writes the bf16 planes straight
-//              into the 128-byte swizzled K-major layout; scales are fetched
-//              one step ahead.  Then the epilogue (tcgen05.ld -> fp32 y).
+//   warps 2-9  transform, two groups of 4 taking alternate K steps (group j
+//              fills plane buffer j): each thread dequantizes an 8 (N) x 8 (K)
+//              unit of codes and writes the bf16 planes straight into the
+//              128-byte swizzled K-major layout; scales are fetched one step
+//              ahead.  Then the epilogue (tcgen05.ld -> fp32 y), group j
+//              draining accumulator j.
 // Included by gemm_tc.cu (shares its device error word).
 #pragma once
 
@@ -27,7 +28,8 @@ namespace wo {
 
 constexpr int BM = 256, BN = 128, BK = 64;  // BK in bf16 elements (128 bytes)
 constexpr int STAGES = 3;
-constexpr int kTransWarps = 16;
+constexpr int kTransWarps = 8;               // two groups of 4
+constexpr int kGroupWarps = kTransWarps / 2;
 constexpr int kThreads = 64 + 32 * kTransWarps;
 constexpr int kAHalf = 128 * BK * 2;      // 16 KB
 constexpr int kAStage = 2 * kAHalf;       // 32 KB
@@ -107,10 +109,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], 1 + kTransWarps);
+      mbar_init(&bars->empty[s], 1 + kGroupWarps);
     }
     for (int j = 0; j < 2; ++j) {
-      mbar_init(&bars->bready[j], kTransWarps);
+      mbar_init(&bars->bready[j], kGroupWarps);
       mbar_init(&bars->bfree[j], 1);
     }
     mbar_init(&bars->accfull, 1);
@@ -168,42 +170,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&bars->accfull);
     }
   } else {
-    // ── transform: all 16 warps work on every K step.  Thread tt handles
-    // two of the 8 columns of one 8 (N) x 8 (K) unit; the 4 threads of a
-    // unit are adjacent lanes, and a warp's 8 units share one 8-row K group.
-    const int tt = threadIdx.x - 64;
-    const int u = tt >> 2, qq = tt & 3;
-    const int n8 = u & 15, k8 = u >> 4;
+    // ── transform: two groups of 4 warps take alternate K steps, group j
+    // filling plane buffer j; one 8 (N) x 8 (K) unit per thread per step ──
+    const int grp = (warp - 2) >> 2;
+    const int t = (threadIdx.x - 64) & 127;
+    const int n8 = t & 15, k8 = t >> 4;  // n-group (16 of 8 columns), k-group (8 of 8 rows)
     const int nsb = N / block;
     const float* sp = ws + (size_t)(n0 + n8 * 8) / block + (size_t)(k8 * 8) * nsb;
     // When the tile's 128 columns share one scale block (block % 128 == 0)
-    // the warp needs 8 scales per step: lane l < 8 loads row l and the
-    // others read it by shuffle.  Otherwise each thread loads its own 8.
-    // Either way one step ahead.
+    // the warp needs only 16 scales per step (its two 8-row K groups): lane
+    // l loads row l % 16 and the others read it by shuffle.  Otherwise each
+    // thread loads its own 8.  Either way one step ahead.
     const bool one_block = block % BN == 0;
-    const float* sp1 = ws + (size_t)n0 / block + (size_t)(k8 * 8 + (lane & 7)) * nsb;
+    const int wrow0 = ((t >> 5) << 4);  // first K row of this warp within a step
+    const float* sp1 = ws + (size_t)n0 / block + (size_t)(wrow0 + (lane & 15)) * nsb;
     float sc_next[8], s1_next = 0.0f;
-    if (one_block) {
-      s1_next = __ldg(sp1);
-    } else {
+    if (grp < ksteps) {
+      if (one_block) {
+        s1_next = __ldg(sp1 + (size_t)(grp * BK) * nsb);
+      } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sc_next[i] = __ldg(sp + (size_t)i * nsb);
+        for (int i = 0; i < 8; ++i) sc_next[i] = __ldg(sp + (size_t)(grp * BK + i) * nsb);
+      }
     }
-    for (int ks = 0; ks < ksteps; ++ks) {
+    for (int ks = grp; ks < ksteps; ks += 2) {
       const int s = ks % STAGES, round = ks / STAGES;
-      const int j = ks & 1, usej = ks >> 1;
+      const int j = grp, usej = ks >> 1;
       float sc[8];
       if (one_block) {
         const float s1 = s1_next;
-        if (ks + 1 < ksteps) s1_next = __ldg(sp1 + (size_t)((ks + 1) * BK) * nsb);
+        if (ks + 2 < ksteps) s1_next = __ldg(sp1 + (size_t)((ks + 2) * BK) * nsb);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sc[i] = __shfl_sync(0xffffffffu, s1, i);
+        for (int i = 0; i < 8; ++i) sc[i] = __shfl_sync(0xffffffffu, s1, ((lane >> 4) << 3) + i);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) sc[i] = sc_next[i];
-        if (ks + 1 < ksteps) {
+        if (ks + 2 < ksteps) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) sc_next[i] = __ldg(sp + (size_t)((ks + 1) * BK + i) * nsb);
+          for (int i = 0; i < 8; ++i) sc_next[i] = __ldg(sp + (size_t)((ks + 2) * BK + i) * nsb);
         }
       }
       if (!mbar_wait_warp(&bars->full[s], round & 1, kErrTimeoutFull)) break;
@@ -218,10 +222,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* phi = sP + (2 * j) * kPlane;
       uint8_t* pmid = sP + (2 * j + 1) * kPlane;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        // column order rotated by n8 so the 8 lanes with the same qq store
-        // to 8 different 16-byte bank groups (r & 7 differs)
-        const int cc = (2 * qq + c + n8) & 7;
+      for (int c = 0; c < 8; ++c) {
+        // rotate the column order by n8 so the lanes of a warp store to 8
+        // different 16-byte bank groups (r & 7 varies across lanes)
+        const int cc = (c + n8) & 7;
         const int r = n8 * 8 + cc;  // N row of the plane
         float w[8];
 #pragma unroll
@@ -245,24 +249,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->bready[j]);
     }
-    // ── epilogue: TMEM -> y; warp (q, idx): M half idx / 2, 64 columns ──
+    // ── epilogue: TMEM -> y ──
     if (mbar_wait_warp(&bars->accfull, 0, kErrTimeoutDone)) {
       tc_fence_after();
-      const int q = warp & 3, idx = (warp - 2) >> 2;
-      const int h = idx >> 1;
-      const int m = m0 + h * 128 + q * 32 + lane;
+      const int q = warp & 3;
+      {
+        const int h = grp;  // accumulator (M half) of this warp's group
+        const int m = m0 + h * 128 + q * 32 + lane;
 #pragma unroll 1
-      for (int cq = 0; cq < 2; ++cq) {
-        const int c = (idx & 1) * 2 + cq;
-        uint32_t r[32];
-        tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + h * BN + c * 32, r);
-        tmem_wait_ld();
-        if (m < M) {
-          float4* o = reinterpret_cast<float4*>(y + (size_t)m * N + n0 + c * 32);
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + h * BN + c * 32, r);
+          tmem_wait_ld();
+          if (m < M) {
+            float4* o = reinterpret_cast<float4*>(y + (size_t)m * N + n0 + c * 32);
 #pragma unroll
-          for (int v = 0; v < 8; ++v)
-            o[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            for (int v = 0; v < 8; ++v)
+              o[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                 __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+          }
         }
       }
     }
