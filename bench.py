@@ -305,28 +305,37 @@ def run_ours(args, world, rank, local):
     a_pin = a_h.pin_memory()
     b_pin = b_h.pin_memory()
 
+    # B's upload runs on a side stream while A is uploaded and quantized; the
+    # packed result comes back into pinned host buffers.
+    side = torch.cuda.Stream(dev)
+    out_words = torch.empty(M * nl // 2 * world, dtype=torch.int32, pin_memory=True)
+    out_scales = torch.empty(M * N // BLOCK, dtype=torch.float32, pin_memory=True)
+    xa = torch.empty(M, K, dtype=torch.float32, device=dev)
+    xb = torch.empty(K, N, dtype=torch.float32, device=dev)
+
     def e2e_step():
-        xa = a_pin.to(dev, non_blocking=True)
-        xb = b_pin.to(dev, non_blocking=True)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            xb.copy_(b_pin, non_blocking=True)
+        xa.copy_(a_pin, non_blocking=True)
         ea = mxb.mx_tensor.quantize(xa, mxb.int8d, BLOCK)
+        torch.cuda.current_stream(dev).wait_stream(side)
         eb = mxb.mx_tensor.quantize(xb, mxb.int8d, BLOCK)
         ec = sharded_qgemm(ea, ShardedQGemmWeight(eb, world, rank))
-        return ec._mx_packed.to("cpu"), ec._mx_scales.to("cpu")
+        out_words.copy_(ec._mx_packed, non_blocking=True)
+        out_scales.copy_(ec._mx_scales, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return out_words, out_scales
 
     for _ in range(2):
         e2e_step()
     barrier(world)
     te = []
-    for _ in range(args.steps):
+    for _ in range(args.steps):  # host wall clock: the caller's view of one call
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
         pk, sc = e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        te.append(e0.elapsed_time(e1))
+        te.append((time.perf_counter() - t0) * 1e3)
     e2e_ms = max_over_ranks(sum(te) / len(te), world)
     h2d = a_h.numel() * 4 + b_h.numel() * 4
     d2h = pk.numel() * pk.element_size() + sc.numel() * 4
