@@ -14,7 +14,7 @@
 constexpr int kClWarps = 8;
 constexpr int kClSplits = 8;   // cluster size along K
 constexpr int kClLB = 8;       // code bytes per lane and row
-constexpr int kClBatch = 8;    // rows per load batch (two batches in flight)
+constexpr int kClBatch = 8;    // rows per load batch
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
