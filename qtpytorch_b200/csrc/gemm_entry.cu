@@ -95,7 +95,7 @@ int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const voi
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   GemvPlan p = gemv_plan(M, K, N, bits, kind, block, w_packed, y);
   if (p.ok) {
-    if (p.ws_bytes && (!workspace || workspace_bytes < p.ws_bytes)) return MXB_E_WORKSPACE;
+    if (!workspace || workspace_bytes < p.ws_bytes) return MXB_E_WORKSPACE;
     return gemv_run(p, x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y,
                     static_cast<float*>(workspace), st);
   }

@@ -267,42 +267,6 @@ int launch_t(int mt, dim3 grid, const XT* x, int M, int K, const uint8_t* W, con
   return MXB_E_DTYPE;
 }
 
-#include "gemv_cluster.cuh"
-
-template <int BITS, int MT, typename XT>
-int launch_cluster_t(int gx, const XT* x, int M, int K, const uint8_t* W, const float* ws, int N,
-                     int block, int krows, float* y, cudaStream_t st) {
-  auto kern = gemv_cluster_kernel<BITS, MT, XT>;
-  const size_t smem = cluster_smem(BITS, MT, krows);
-  MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)gx, kClSplits, 1);
-  cfg.blockDim = dim3(kClWarps * 32, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = kClSplits;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  MXB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, x, M, K, W, ws, N, block, krows, y));
-  MXB_LAUNCH_CHECK();
-  return MXB_OK;
-}
-
-template <typename XT>
-int launch_cluster(int bits, int mt, const XT* x, int M, int K, const uint8_t* W,
-                   const float* ws, int N, int block, int krows, float* y, cudaStream_t st) {
-  const int gx = (int)cdiv(N, 32 * (kClLB * 8 / bits));
-  if (bits == 4)
-    return mt == 1 ? launch_cluster_t<4, 1, XT>(gx, x, M, K, W, ws, N, block, krows, y, st)
-                   : launch_cluster_t<4, 2, XT>(gx, x, M, K, W, ws, N, block, krows, y, st);
-  return mt == 1 ? launch_cluster_t<8, 1, XT>(gx, x, M, K, W, ws, N, block, krows, y, st)
-                 : launch_cluster_t<8, 2, XT>(gx, x, M, K, W, ws, N, block, krows, y, st);
-}
-
 int wide_cpt(int bits, int lb) { return lb * 8 / bits; }
 
 size_t wide_smem(int mt, int krows, int cols) {
@@ -347,19 +311,6 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
   if (N % kCols || block % kCols || N % block) return p;
   if (((uintptr_t)w % (uintptr_t)bits) || ((uintptr_t)y % 16)) return p;
   const int mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16;
-  if (kind == MXB_KIND_INT && (bits == 4 || bits == 8) && mt <= 2) {
-    const int cpt = kClLB * 8 / bits;
-    if (N % cpt == 0 && block % cpt == 0 && ((uintptr_t)w % kClLB) == 0) {
-      // cluster kernel: 8 K-slices per cluster reduce in distributed shared
-      // memory; no workspace
-      p.ok = true;
-      p.kernel = 3;
-      p.splits = kClSplits;
-      p.krows = (int)(cdiv(cdiv(K, kClSplits), 8) * 8);
-      p.ws_bytes = 0;
-      return p;
-    }
-  }
   if (kind == MXB_KIND_INT && (bits == 4 || bits == 8)) {
     const int lb = mt <= 2 ? 16 : (bits == 4 ? 4 : 8);
     const int cpt = wide_cpt(bits, lb);
@@ -401,15 +352,6 @@ int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_
   dim3 grid((unsigned)cdiv(N, kCtaCols), (unsigned)plan.splits);
   const uint8_t* W = static_cast<const uint8_t*>(w);
   int rc;
-  if (plan.kernel == 3) {
-    if (x_dtype == MXB_F32)
-      return launch_cluster(bits, mt, static_cast<const float*>(x), (int)M, (int)K, W, ws, (int)N,
-                            block, plan.krows, y, st);
-    if (x_dtype == MXB_BF16)
-      return launch_cluster(bits, mt, static_cast<const __nv_bfloat16*>(x), (int)M, (int)K, W, ws,
-                            (int)N, block, plan.krows, y, st);
-    return MXB_E_DTYPE;
-  }
   if (plan.kernel == 1) {
     dim3 g2((unsigned)cdiv(N, 32 * wide_cpt(bits, plan.lb)), (unsigned)plan.splits);
     if (x_dtype == MXB_F32) {

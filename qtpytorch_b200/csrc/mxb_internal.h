@@ -26,8 +26,7 @@ struct GemvPlan {
   int splits;       // K splits
   int krows;        // rows of K per split
   size_t ws_bytes;  // partial-sum workspace
-  int kernel = 0;   // 0: 8 columns per thread, any code width; 1: wide loads (int4/int8);
-                    // 3: cluster kernel (int4/int8, M <= 2, no workspace)
+  int kernel = 0;   // 0: 8 columns per thread, any code width; 1: wide loads (int4/int8)
   int lb = 0;       // kernel 1: code bytes per thread and row (4, 8 or 16)
 };
 GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,

@@ -44,9 +44,7 @@ def test_version_and_sizes():
     assert lib.mxb_packed_bytes(10, 3, 128) == 0
     assert lib.mxb_quantize_workspace_size(4096, 64, 4, 0, 0, 128) == 0
     assert lib.mxb_quantize_workspace_size(700, 90, 4, 0, 0, 100) == 7 * 4
-    # M <= 2 int4/int8 runs the cluster GEMV (no workspace); larger M split-K
-    assert lib.mxb_linear_wonly_workspace_size(1, 4096, 11008, 4, 0, 128, 0) == 0
-    assert lib.mxb_linear_wonly_workspace_size(4, 4096, 11008, 4, 0, 128, 0) > 0
+    assert lib.mxb_linear_wonly_workspace_size(1, 4096, 11008, 4, 0, 128, 0) > 0
 
 
 def test_argument_errors_need_no_gpu():
