@@ -1,8 +1,9 @@
 // Inline-PTX helpers for sm_100a: mbarriers, TMA tensor loads, tcgen05
 // (TMEM allocation, MMA, commit, loads) and shared-memory descriptors.
 //
-// Every wait is bounded: after kSpinLimit polls it records an error code in
-// `g_mxb_device_error` and returns false, so a kernel never hangs the GPU.
+// Every wait is bounded: after 2 s of wall time (%globaltimer) or kSpinLimit
+// polls it records an error code in `g_mxb_device_error` and returns false,
+// so a kernel never hangs the GPU.
 #pragma once
 
 #include <cuda.h>
@@ -15,6 +16,7 @@ namespace mxb {
 // mxb_device_error() reads and clears it.
 
 constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 enum DeviceError : int {
   kErrTimeoutFull = 1,
@@ -62,10 +64,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
+// Non-blocking probe of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with the given parity to complete: gives up
+// after kWaitLimitNs of wall time (or kSpinLimit polls), records err_code and
+// returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int err_code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_test_wait(bar, parity)) return true;  // already complete: no blocking probe
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15) == 15 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
   atomicCAS(&g_mxb_device_error, 0, err_code);
   return false;
 }
