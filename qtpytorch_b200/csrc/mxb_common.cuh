@@ -57,23 +57,26 @@ __device__ __constant__ static const uint32_t kF4Grid[16] = {
 __device__ __forceinline__ float f4_grid(int idx) { return __uint_as_float(kF4Grid[idx & 15]); }
 
 // bucketize(v, mids, right=False) == number of boundaries strictly below v.
+// The 15 boundaries are symmetric: -p6..-p0, 0, p0..p6 with p = 1/24, 1/8,
+// 5/24, 7/24, 5/12, 7/12, 5/6 (each the fp32 midpoint of adjacent grid
+// values).  For v > 0 the count is 8 + #(p < v); for v <= 0 (and -0) it is
+// 7 - #(p <= |v|), and p <= a <=> p < nextup(a) for finite a >= 0.  The
+// count over the seven p is a three-step branchless binary search.  NaN ->
+// 15, as torch.bucketize places NaN last.
 __device__ __forceinline__ int f4_bucket(float v) {
-  // boundaries: -5/6, -7/12, -5/12, -7/24, -5/24, -1/8, -1/24, 0, 1/24, 1/8,
-  // 5/24, 7/24, 5/12, 7/12, 5/6 (each the fp32 midpoint of adjacent grid values)
-  const float m0 = __uint_as_float(0xbf555556u), m1 = __uint_as_float(0xbf155556u),
-              m2 = __uint_as_float(0xbed55556u), m3 = __uint_as_float(0xbe955556u),
-              m4 = __uint_as_float(0xbe555556u), m5 = -0.125f,
-              m6 = __uint_as_float(0xbd2aaaabu), m7 = 0.0f,
-              m8 = __uint_as_float(0x3d2aaaabu), m9 = 0.125f,
-              m10 = __uint_as_float(0x3e555556u), m11 = __uint_as_float(0x3e955556u),
-              m12 = __uint_as_float(0x3ed55556u), m13 = __uint_as_float(0x3f155556u),
-              m14 = __uint_as_float(0x3f555556u);
-  // !(v <= m) == (v > m) for numbers; NaN counts past every boundary (-> 15),
-  // as torch.bucketize places NaN last
-  int i = !(v <= m0) + !(v <= m1) + !(v <= m2) + !(v <= m3) + !(v <= m4) + !(v <= m5) +
-          !(v <= m6) + !(v <= m7) + !(v <= m8) + !(v <= m9) + !(v <= m10) + !(v <= m11) +
-          !(v <= m12) + !(v <= m13) + !(v <= m14);
-  return i;
+  const float p0 = __uint_as_float(0x3d2aaaabu), p1 = 0.125f,
+              p2 = __uint_as_float(0x3e555556u), p3 = __uint_as_float(0x3e955556u),
+              p4 = __uint_as_float(0x3ed55556u), p5 = __uint_as_float(0x3f155556u),
+              p6 = __uint_as_float(0x3f555556u);
+  const bool neg = (__float_as_uint(v) >> 31) != 0u;
+  const float a = fminf(fabsf(v), 2.0f);  // every p < 2; NaN handled below
+  const float x = neg ? __uint_as_float(__float_as_uint(a) + 1u) : a;
+  int c = (p3 < x) ? 4 : 0;
+  c += (((c & 4) ? p5 : p1) < x) ? 2 : 0;
+  const float pl = (c & 4) ? ((c & 2) ? p6 : p4) : ((c & 2) ? p2 : p0);
+  c += (pl < x) ? 1 : 0;
+  const int i = neg ? 7 - c : 8 + c - (a == 0.0f ? 1 : 0);
+  return v == v ? i : 15;
 }
 
 // Sign-extend the low `bits` bits of v.

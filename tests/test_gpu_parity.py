@@ -72,6 +72,51 @@ def test_quantize_specials():
         assert np.array_equal(_u32(q._mx_scales.cpu().numpy()), _u32(s)), dt
 
 
+def _float4_edge_input():
+    """Rows of 128 whose quotients x / amax land exactly on, and one ulp either
+    side of, each float4 bucket boundary (both signs), plus +-0, denormals,
+    quotients that underflow to zero, and blocks holding inf / NaN."""
+    # the fp32 midpoints of adjacent grid values, as the kernels compare them
+    grid = np.array([0, 1, 2, 3, 4, 6, 8, 12], dtype=np.float32) / np.float32(12)
+    mids = ((grid[:-1] + grid[1:]) * np.float32(0.5)).astype(np.float32)
+    up = np.nextafter(mids, np.float32(np.inf))
+    dn = np.nextafter(mids, np.float32(0))
+    vals = np.concatenate([mids, up, dn]).astype(np.float32)
+    vals = np.concatenate([vals, -vals, np.float32([0.0, -0.0, 1e-45, -1e-45, 1e-38, -1e-38])])
+    rows = []
+    for amax in (1.0, 3.0, 0.7, 1e-20, 2.0 ** 100):
+        r = np.zeros(128, dtype=np.float32)
+        r[0] = amax
+        v = (vals.astype(np.float64) * amax).astype(np.float32)
+        r[1:1 + len(v)] = v
+        rows.append(r)
+    r = np.zeros(128, dtype=np.float32)
+    r[0] = 2.0 ** 100
+    r[1:8] = [1e-45, -1e-45, 3e-45, 1e-40, -1e-40, 1e-38, 0.0]
+    rows.append(r)
+    r = np.linspace(-2, 2, 128).astype(np.float32)
+    r[7] = np.inf
+    r[9] = -np.inf
+    rows.append(r)
+    r = np.linspace(-2, 2, 128).astype(np.float32)
+    r[4] = np.nan
+    rows.append(r)
+    return np.stack(rows)
+
+
+def test_float4_bucket_boundaries():
+    x = _float4_edge_input()
+    d = get_mx_dtype("float4d")
+    q = mxb.mx_tensor.quantize(torch.from_numpy(x).cuda(), d, 128)
+    p, s, _ = O.quantize(x, d.bits, d.kind, 128)
+    assert np.array_equal(q._mx_packed.cpu().numpy(), p)
+    # bit-exact scales; a NaN block's scale is NaN (its payload is not compared)
+    gs = q._mx_scales.cpu().numpy()
+    nan = np.isnan(s)
+    assert np.array_equal(np.isnan(gs), nan)
+    assert np.array_equal(_u32(gs[~nan]), _u32(s[~nan]))
+
+
 @pytest.mark.parametrize("c", [c for c in cases.QUANT_CASES if "h_" in c["key"]],
                          ids=lambda c: c["key"])
 def test_hadamard_rotation_matches_reference(golden, c):
