@@ -152,7 +152,10 @@ size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits
  *   x        [M, K] of x_dtype (MXB_F32 / MXB_BF16)
  *   w_packed / w_scales  the mx_tensor storage of W^T
  *   y        [M, N] fp32
- * M <= 16 runs a split-K GEMV on the CUDA cores; larger M the tcgen05 GEMM.
+ * Small M (decode) runs split-K: with bf16 x, integer codes and
+ * block % 128 == 0, a tcgen05 kernel for 3 <= M <= 32 (the block scale
+ * applied to x, the codes used as exact bf16 MMA operands); otherwise, for
+ * M <= 16, a GEMV on the CUDA cores.  Larger M runs the tcgen05 GEMM.
  */
 int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const void* w_packed,
                      const float* w_scales, int64_t N, int bits, int kind, int block,
@@ -160,16 +163,17 @@ int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const voi
                      void* stream);
 
 /*
- * The decode (M <= 16) weight-only linear of mxb_linear_wonly, for callers
+ * The decode (small-M) weight-only linear of mxb_linear_wonly, for callers
  * that cannot allocate device memory when they run the layer: runtimes that
  * only use buffers planned ahead of time, code inside a fixed memory pool,
  * or foreign-language hosts without a CUDA allocator.  It takes no
  * workspace; the split-K partial sums go to a 16 MiB array inside the
  * library (every GPU that loads the library keeps it until exit).
  * It has no counterpart in the reference; it exists only for such callers.
- *   Same arguments and result as mxb_linear_wonly for the GEMV shapes
- *   (1 <= M <= 16, N % 8 == 0, N % block == 0, block % 8 == 0); other shapes
- *   return MXB_E_SHAPE.  Shapes whose partial sums cannot fit 16 MiB even
+ *   Same arguments and result as mxb_linear_wonly for the split-K shapes
+ *   (1 <= M <= 16, N % 8 == 0, N % block == 0, block % 8 == 0; with bf16 x,
+ *   integer codes, block % 128 == 0, N % 128 == 0 and K % 64 == 0 also
+ *   M up to 32); other shapes return MXB_E_SHAPE.  Shapes whose partial sums cannot fit 16 MiB even
  *   with 256-row K splits (splits * M * N * 4 bytes) return MXB_E_WORKSPACE.
  *   The first call on each device looks the array up (with that device
  *   current); make that first call before any stream capture.  All calls

@@ -76,7 +76,7 @@ size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits
                                        int block, int mode) {
   (void)mode;
   if (M <= 0 || K <= 0 || N <= 0) return 0;
-  GemvPlan p = gemv_plan(M, K, N, bits, kind, block, nullptr, nullptr);
+  GemvPlan p = gemv_plan(M, K, N, bits, kind, block, nullptr, nullptr, -1, nullptr);
   return p.ok ? p.ws_bytes : 0;
 }
 
@@ -93,7 +93,7 @@ int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const voi
     return MXB_E_SHAPE;
   if (!x || !w_packed || !w_scales || !y) return MXB_E_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  GemvPlan p = gemv_plan(M, K, N, bits, kind, block, w_packed, y);
+  GemvPlan p = gemv_plan(M, K, N, bits, kind, block, w_packed, y, x_dtype, x);
   if (p.ok) {
     if (!workspace || workspace_bytes < p.ws_bytes) return MXB_E_WORKSPACE;
     return gemv_run(p, x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y,

@@ -28,6 +28,7 @@ __device__ int g_mxb_device_error = 0;
 
 #include "tc_ptx.cuh"
 #include "wonly_tc.cuh"
+#include "wonly_dec.cuh"
 
 namespace mxb {
 
@@ -415,6 +416,68 @@ int tc_wonly(const void* x, int64_t M, int64_t K, const void* w, const float* ws
     case 2: return wonly_mode<2, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
     case 4: return wonly_mode<4, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
     case 8: return wonly_mode<8, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
+  }
+  return MXB_E_DTYPE;
+}
+
+// ── decode-regime weight-only linear (wonly_dec.cuh) ─────────────────────────
+bool tc_dec_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w, int64_t N,
+                     int bits, int kind, int block) {
+  if (x_dtype != MXB_BF16 || kind != MXB_KIND_INT) return false;
+  if (!(bits == 1 || bits == 2 || bits == 4 || bits == 8)) return false;
+  // M <= 2 stays on the CUDA-core GEMV, which streams the weight faster when
+  // there is at most two rows of work per code
+  if (M < 3 || M > 32 || K % dec::BK || N % dec::BN || block % dec::BN || N % block) return false;
+  if (((uintptr_t)x | (uintptr_t)w) & 15) return false;
+  return true;
+}
+
+void tc_dec_plan(int64_t K, int64_t N, int* splits, int* kc) {
+  // one wave of about two CTAs per SM: 128-column groups x K splits
+  const int64_t groups = N / dec::BN, steps = K / dec::BK;
+  int64_t sp = (2 * kSMs) / groups;
+  if (sp < 1) sp = 1;
+  if (sp > steps) sp = steps;
+  int64_t c = cdiv(steps, sp) * dec::BK;
+  if (c > dec::kMaxKc) c = dec::kMaxKc;
+  *kc = (int)c;
+  *splits = (int)cdiv(K, c);
+}
+
+template <int BITS, int MP>
+static int dec_launch(const CUtensorMap& tw, const __nv_bfloat16* x, const float* ws, int M,
+                      int N, int K, int block, int kc, int splits, float* out, cudaStream_t st) {
+  auto kern = dec::wonly_dec_kernel<BITS, MP>;
+  const size_t smem = dec::smem_bytes<BITS, MP>(kc);
+  MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((unsigned)(N / dec::BN), (unsigned)splits);
+  kern<<<grid, dec::kThreads, smem, st>>>(tw, x, ws, M, N, K, block, kc, out);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+template <int BITS>
+static int dec_mp(const CUtensorMap& tw, const __nv_bfloat16* x, const float* ws, int M, int N,
+                  int K, int block, int kc, int splits, float* out, cudaStream_t st) {
+  return M <= 16 ? dec_launch<BITS, 16>(tw, x, ws, M, N, K, block, kc, splits, out, st)
+                 : dec_launch<BITS, 32>(tw, x, ws, M, N, K, block, kc, splits, out, st);
+}
+
+int tc_wonly_dec(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
+                 int bits, int block, int kc, int splits, float* out, cudaStream_t st) {
+  if (kc <= 0 || kc % dec::BK || kc > dec::kMaxKc || (int64_t)splits * kc < K) return MXB_E_ARG;
+  CUtensorMap tw;
+  const uint64_t row_bytes = (uint64_t)N * bits / 8;
+  if (make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, row_bytes, (uint64_t)K,
+                   (uint32_t)(dec::BN * bits / 8), dec::BK, CU_TENSOR_MAP_SWIZZLE_NONE) != MXB_OK)
+    return MXB_E_CUDA;
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  const int iM = (int)M, iN = (int)N, iK = (int)K;
+  switch (bits) {
+    case 1: return dec_mp<1>(tw, xb, ws, iM, iN, iK, block, kc, splits, out, st);
+    case 2: return dec_mp<2>(tw, xb, ws, iM, iN, iK, block, kc, splits, out, st);
+    case 4: return dec_mp<4>(tw, xb, ws, iM, iN, iK, block, kc, splits, out, st);
+    case 8: return dec_mp<8>(tw, xb, ws, iM, iN, iK, block, kc, splits, out, st);
   }
   return MXB_E_DTYPE;
 }

@@ -305,8 +305,25 @@ int launch_wide(int mt, int lb, dim3 grid, const XT* x, int M, int K, const uint
 namespace mxb {
 
 GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,
-                   const void* w, const void* y) {
+                   const void* w, const void* y, int x_dtype, const void* x) {
   GemvPlan p{false, 0, 0, 0};
+  if (x_dtype < 0) {  // workspace query: the larger of the bf16 and fp32 plans
+    GemvPlan a = gemv_plan(M, K, N, bits, kind, block, w, y, MXB_BF16, nullptr);
+    GemvPlan b = gemv_plan(M, K, N, bits, kind, block, w, y, MXB_F32, nullptr);
+    return a.ws_bytes >= b.ws_bytes ? a : b;
+  }
+  if (M >= 1 && K >= 1 && ((uintptr_t)y % 16) == 0 &&
+      tc_dec_eligible(x, x_dtype, M, K, w, N, bits, kind, block)) {
+    int splits, kc;
+    tc_dec_plan(K, N, &splits, &kc);
+    p.ok = true;
+    p.kernel = 4;
+    p.splits = splits;
+    p.krows = kc;
+    p.max_krows = kDecMaxKc;
+    p.ws_bytes = splits > 1 ? (size_t)splits * M * N * sizeof(float) : 0;
+    return p;
+  }
   if (M < 1 || M > 16 || K < 1 || N < kCols) return p;
   if (N % kCols || block % kCols || N % block) return p;
   if (((uintptr_t)w % (uintptr_t)bits) || ((uintptr_t)y % 16)) return p;
@@ -325,6 +342,7 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
       splits = cdiv(K, krows);
       p.ok = true;
       p.kernel = 1;
+      p.max_krows = 1024;
       p.lb = lb;
       p.splits = (int)splits;
       p.krows = (int)krows;
@@ -341,6 +359,7 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
   p.ok = true;
   p.splits = (int)splits;
   p.krows = (int)krows;
+  p.max_krows = kMaxRows;
   p.ws_bytes = (size_t)splits * M * N * sizeof(float);
   return p;
 }
@@ -352,7 +371,12 @@ int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_
   dim3 grid((unsigned)cdiv(N, kCtaCols), (unsigned)plan.splits);
   const uint8_t* W = static_cast<const uint8_t*>(w);
   int rc;
-  if (plan.kernel == 1) {
+  if (plan.kernel == 4) {
+    if (x_dtype != MXB_BF16 || plan.krows > plan.max_krows) return MXB_E_ARG;
+    rc = tc_wonly_dec(x, M, K, w, ws, N, bits, block, plan.krows, plan.splits,
+                      plan.splits > 1 ? partial : y, st);
+    if (rc != MXB_OK || plan.splits == 1) return rc;
+  } else if (plan.kernel == 1) {
     dim3 g2((unsigned)cdiv(N, 32 * wide_cpt(bits, plan.lb)), (unsigned)plan.splits);
     if (x_dtype == MXB_F32) {
       const float* xf = static_cast<const float*>(x);

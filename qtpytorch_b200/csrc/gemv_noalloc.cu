@@ -63,11 +63,12 @@ extern "C" int mxb_linear_wonly_noalloc(const void* x, int x_dtype, int64_t M, i
   if (K * N >= (int64_t)1 << 31) return MXB_E_SHAPE;
   if (!x || !w_packed || !w_scales || !y) return MXB_E_ARG;
 
-  mxb::GemvPlan plan = mxb::gemv_plan(M, K, N, bits, kind, block, w_packed, y);
-  if (!plan.ok) return MXB_E_SHAPE;  // not a split-K GEMV shape (M <= 16 etc.)
+  mxb::GemvPlan plan = mxb::gemv_plan(M, K, N, bits, kind, block, w_packed, y, x_dtype, x);
+  if (!plan.ok) return MXB_E_SHAPE;  // not a split-K (decode) shape
   // Fewer, longer K splits until the partial sums fit the fixed scratch.
-  while (plan.ws_bytes > kScratchBytes && plan.krows < kMaxRowsPerSplit) {
-    int64_t krows = plan.krows * 2 > kMaxRowsPerSplit ? kMaxRowsPerSplit : plan.krows * 2;
+  const int max_rows = plan.max_krows < kMaxRowsPerSplit ? plan.max_krows : kMaxRowsPerSplit;
+  while (plan.ws_bytes > kScratchBytes && plan.krows < max_rows) {
+    int64_t krows = plan.krows * 2 > max_rows ? max_rows : plan.krows * 2;
     plan.krows = (int)krows;
     plan.splits = (int)mxb::cdiv(K, krows);
     plan.ws_bytes = (size_t)plan.splits * M * N * sizeof(float);

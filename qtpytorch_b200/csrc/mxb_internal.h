@@ -21,16 +21,21 @@ int wonly_generic(const void* x, int x_dtype, int64_t M, int64_t K, const void* 
                   cudaStream_t st);
 
 // gemv.cu
+constexpr int kDecMaxKc = 2048;  // K rows per CTA of the tcgen05 decode kernel
 struct GemvPlan {
   bool ok;          // shape/alignment supported by the split-K kernel
   int splits;       // K splits
   int krows;        // rows of K per split
   size_t ws_bytes;  // partial-sum workspace
-  int kernel = 0;   // 0: 8 columns per thread, any code width; 1: wide loads (int4/int8)
+  int kernel = 0;   // 0: 8 columns per thread, any code width; 1: wide loads (int4/int8);
+                    // 4: tcgen05 decode kernel (bf16 x, integer codes, 3 <= M <= 32)
   int lb = 0;       // kernel 1: code bytes per thread and row (4, 8 or 16)
+  int max_krows = 0;  // largest rows per split the kernel accepts
 };
+// x_dtype < 0: the dtype is not known yet (workspace queries); the plan then
+// covers the largest workspace either activation dtype may need.
 GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,
-                   const void* w, const void* y);
+                   const void* w, const void* y, int x_dtype, const void* x);
 int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_t K,
              const void* w, const float* ws, int64_t N, int bits, int kind, int block,
              float* y, float* partial, cudaStream_t st);
@@ -47,5 +52,10 @@ bool tc_wonly_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const v
                        int64_t N, int bits, int kind, int block, const float* y);
 int tc_wonly(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
              int bits, int kind, int block, int mode, float* y, cudaStream_t st);
+bool tc_dec_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w, int64_t N,
+                     int bits, int kind, int block);
+void tc_dec_plan(int64_t K, int64_t N, int* splits, int* kc);
+int tc_wonly_dec(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
+                 int bits, int block, int kc, int splits, float* out, cudaStream_t st);
 
 }  // namespace mxb

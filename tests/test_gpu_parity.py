@@ -11,6 +11,7 @@ import torch
 import cases
 import qtpytorch_b200 as mxb
 from oracle import mx_oracle as O
+from qtpytorch_b200 import _lib as L
 from qtpytorch_b200 import ops
 from qtpytorch_b200.dtypes import get_mx_dtype
 
@@ -179,7 +180,7 @@ def test_mx_linear_matches_reference(golden, c):
     assert np.all(np.abs(yr - y64) <= LIN_TOL * bound + 1e-30)
 
 
-@pytest.mark.parametrize("M", [1, 3, 16, 17, 64, 128])
+@pytest.mark.parametrize("M", [1, 3, 16, 17, 32, 64, 128])
 @pytest.mark.parametrize("dt", ["int4d", "int8d", "int2d", "int1d", "float4d"])
 def test_linear_shapes(M, dt):
     d = get_mx_dtype(dt)
@@ -193,4 +194,25 @@ def test_linear_shapes(M, dt):
     y = ml(x.cuda()).cpu().numpy()
     pw, sw, _ = O.quantize(w.t().contiguous().numpy(), d.bits, d.kind, 128)
     wdq = O.dequantize(pw, sw, d.bits, d.kind, (256, 384), 128)
+    _linear_check(y, x.float().numpy(), wdq)
+
+
+@pytest.mark.parametrize("M", [3, 5, 24, 32])
+@pytest.mark.parametrize("dt", ["int4d", "int8d", "int2d", "int1d"])
+def test_decode_tc_uneven_k(M, dt):
+    """Decode shapes on the tcgen05 split-K kernel with a K (17 steps of 64)
+    that does not divide evenly into the K chunks, block 256."""
+    d = get_mx_dtype(dt)
+    g = torch.Generator().manual_seed(100 + M)
+    K, N = 1088, 640
+    w = torch.randn(N, K, generator=g) * 0.02
+    x = torch.randn(M, K, generator=g).bfloat16()
+    lin = torch.nn.Linear(K, N, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    ml = mxb.mx_linear.from_linear(lin.cuda(), d, 256)
+    y = ml(x.cuda()).cpu().numpy()
+    assert L.load().mxb_device_error(1) == 0
+    pw, sw, _ = O.quantize(w.t().contiguous().numpy(), d.bits, d.kind, 256)
+    wdq = O.dequantize(pw, sw, d.bits, d.kind, (K, N), 256)
     _linear_check(y, x.float().numpy(), wdq)
