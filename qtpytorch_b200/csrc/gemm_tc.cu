@@ -11,7 +11,7 @@
 //               two TMEM accumulators, so the MMAs of K-block kb+1 overlap
 //               the promotion of kb;
 //   warps 2..17 promotion: tcgen05.ld the int32 tile (one TMEM lane = one
-//               row, 32 columns per warp), convert exactly, apply both
+//               row, 32 columns per warp), convert exactly (I2F), apply both
 //               scales and add into fp32 registers (packed f32x2 ops), one rounding per
 //               step.  The fp32 accumulator is bit-identical to the
 //               reference's.
@@ -151,7 +151,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* sbrow = sb + n0 + col0 + lane;
     float sa_next = __ldg(sap);
     float sb_next = __ldg(sbrow);
-    const uint64_t magic2 = pack2(12582912.0f, 12582912.0f);
     for (int kb = 0; kb < kbn; ++kb) {
       const int b = kb & 1, use = kb >> 1;
       const float sa_v = sa_next;
@@ -179,11 +178,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int c = c4 * 4 + 2 * j;
-          // exact int -> fp32 for |p| < 2^22: 1.5 * 2^23 + p holds p in its
-          // low mantissa bits; |P| <= 128 * 127^2 < 2^22
-          const uint64_t biased = pack2(__int_as_float(0x4B400000 + (int)r[c]),
-                                        __int_as_float(0x4B400000 + (int)r[c + 1]));
-          const uint64_t pf = fsub2(biased, magic2);
+          // int -> fp32 is exact (|P| <= 128 * 128^2 < 2^24); the conversion
+          // runs outside the FMA pipe, which the three FP32 operations keep busy
+          const uint64_t pf = pack2(__int2float_rn((int)r[c]), __int2float_rn((int)r[c + 1]));
           // products packed; the add stays scalar so it is never fused
           // with the multiply (a fused add would skip one rounding)
           const float2 t = unpack2(fmul2(fmul2(pf, sa2), sv[j]));
