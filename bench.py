@@ -432,6 +432,27 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
         out[f"quantize_{dt}_fp32_2^{n.bit_length() - 1}"] = {
             "ms": t, "gbs": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / hbm}
         del x
+    # configs[3] on one rank: int4dh weight-only linear, W 8192 x 8192 ~ N(0, 0.02)
+    # with 8 outlier input channels x25, x bf16 [4096, 8192]; the sharded
+    # linear at world 1 (GEMM + the 8192-point unrotation of y)
+    from qtpytorch_b200 import parallel as P
+    g3 = torch.Generator().manual_seed(3)
+    W3 = torch.randn(8192, 8192, generator=g3) * 0.02
+    W3[:, torch.randperm(8192, generator=g3)[:8]] *= 25.0
+    lin3 = torch.nn.Linear(8192, 8192, bias=False)
+    with torch.no_grad():
+        lin3.weight.copy_(W3)
+    ml3 = mxb.mx_linear.from_linear(lin3.to(dev), mxb.get_mx_dtype("int4dh"), 128)
+    del W3, lin3
+    x3 = torch.randn(4096, 8192, generator=torch.Generator().manual_seed(4)).bfloat16().to(dev)
+    sw3 = P.ShardedLinearWeight.from_module(ml3, 1, 0)
+    for _ in range(2):
+        P.sharded_linear(x3, sw3)
+    fn = graphed(lambda: P.sharded_linear(x3, sw3), stream)
+    t = statistics.median(time_steps(fn, steps, flush, stream))
+    flops = 2.0 * 4096 * 8192 * 8192
+    out["wonly_int4dh_8192_M4096_g1"] = {"ms": t, "tflops": flops / t / 1e9,
+                                         "tensor_frac_bf16": flops / t / 1e9 / bf16}
     return out
 
 

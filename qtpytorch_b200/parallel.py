@@ -10,7 +10,12 @@
 The packed matmul keeps the reference's B-scale view (b_scales viewed
 [K/block, N], mxtorch.py:1354-1355): a rank's shard of that view is
 ``b_scales.view(K/block, N)[:, n0:n1]``, so sharded results are identical to
-the single-GPU ones.
+the single-GPU ones.  The weight-only linear stores W^T [K, N] quantized flat
+with N % block == 0, so a shard of whole blocks is the column range of every
+row's codes and of the scale matrix s[k, n / block]; ``h`` dtypes are
+unrotated along the full rows of y after the gather.  Shards may differ by
+one block (11008 = 86 blocks over 8 ranks): the gather pads every shard to
+the widest one.
 """
 from __future__ import annotations
 
@@ -79,11 +84,67 @@ def sharded_qgemm(qa: mx_tensor, w: ShardedQGemmWeight,
                                       nl, 8, w.block, out_dt.bits)
     if w.world == 1:
         return mx_tensor(c_packed, c_scales, out_dt, torch.Size([M, w.N]), M * w.N, w.block)
-    widths = {b - a for a, b in w.shards}
-    if len(widths) != 1:
-        raise NotImplementedError("uneven column shards need a variable-size gather")
-    words, scales = gather_columns(c_packed, c_scales, M, w.world, group)
+    words, scales = gather_columns(c_packed, c_scales, M, w.world, group,
+                                   widths=[b - a for a, b in w.shards], bits=out_dt.bits,
+                                   block=w.block)
     return mx_tensor(words, scales, out_dt, torch.Size([M, w.N]), M * w.N, w.block)
+
+
+class ShardedLinearWeight:
+    """The column shard of an ``mx_linear`` weight (W^T [K, N] quantized flat,
+    any code width) held by one rank: whole ``block``-column groups, so the
+    shard is a column range of every row's codes and of s[k, n / block]."""
+
+    def __init__(self, w: mx_tensor, world: int, rank: int):
+        K, N = w._mx_orig_shape
+        self.K, self.N, self.world, self.rank = K, N, world, rank
+        self.block = w._mx_block
+        self.dtype = w._mx_dtype
+        if N % self.block or self.block % 8:
+            raise ValueError("column sharding needs N % block == 0 and block % 8 == 0")
+        self.shards = column_shards(N, world, max(self.block, 128))
+        n0, n1 = self.shards[rank]
+        self.n0, self.n1 = n0, n1
+        bits = self.dtype.bits
+        row = N * bits // 8
+        self.codes = (w._mx_packed.view(torch.uint8)[: K * row].view(K, row)
+                      [:, n0 * bits // 8: n1 * bits // 8].contiguous())
+        nsb = N // self.block
+        self.scales = (w._mx_scales[: K * nsb].view(K, nsb)
+                       [:, n0 // self.block: n1 // self.block].contiguous())
+
+    @classmethod
+    def from_module(cls, m, world: int, rank: int) -> "ShardedLinearWeight":
+        return cls(m._mx_weight, world, rank)
+
+
+def sharded_linear(x: torch.Tensor, w: ShardedLinearWeight, group=None, mode: str = "parity",
+                   out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """y = x @ dequant(W^T) with W^T column-sharded over the ranks of
+    ``group`` (x replicated on every rank).  Each rank computes y[:, n0:n1]
+    with the single-GPU kernel, then one all-gather assembles y; for ``h``
+    dtypes the full rows are unrotated afterwards.  ``out_dtype`` bf16 casts
+    before the gather (half the bytes on NVLink) unless the rows still need
+    the fp32 unrotation."""
+    from . import _lib as L
+    lead = x.shape[:-1]
+    K = x.shape[-1]
+    if K != w.K:
+        raise ValueError("inner dimensions differ")
+    xm = x.reshape(-1, K)
+    M = xm.shape[0]
+    md = L.MODE_FAST if mode == "fast" else L.MODE_PARITY
+    y = ops.linear_wonly(xm, w.codes, w.scales, K, w.n1 - w.n0, w.dtype, w.block, md)
+    h = w.dtype.is_hadamard
+    if out_dtype == torch.bfloat16 and not h:
+        y = y.bfloat16()
+    if w.world > 1:
+        y = gather_dense_columns(y, M, w.world, [b - a for a, b in w.shards], group)
+    if h:
+        y = ops.hadamard_rows(y, w.dtype.hadamard_seed, inverse=True)
+        if out_dtype == torch.bfloat16:
+            y = y.bfloat16()
+    return y.reshape(*lead, w.N)
 
 
 def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
@@ -96,20 +157,48 @@ def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
     return out
 
 
+def _gather_rows_var(t: torch.Tensor, M: int, world: int, widths: List[int], group):
+    """t [M, widths[rank]] on each rank -> [M, sum(widths)] (columns in rank
+    order): every shard is padded to the widest, gathered once, then each
+    rank's valid columns are concatenated per row."""
+    wmax = max(widths)
+    t = t.reshape(M, -1)
+    if t.shape[1] < wmax:
+        t = torch.cat([t, t.new_zeros(M, wmax - t.shape[1])], dim=1)
+    g = _all_gather(t.contiguous(), world, group)  # [G, M, wmax]
+    if all(w == wmax for w in widths):
+        return g.transpose(0, 1).reshape(M, -1)
+    return torch.cat([g[r, :, : widths[r]] for r in range(world)], dim=1)
+
+
+def gather_dense_columns(y: torch.Tensor, M: int, world: int, widths: List[int],
+                         group=None) -> torch.Tensor:
+    """Assemble y [M, N] from the ranks' column shards y[:, n0:n1]."""
+    return _gather_rows_var(y, M, world, widths, group)
+
+
 def gather_columns(c_packed: torch.Tensor, c_scales: torch.Tensor, M: int, world: int,
-                   group=None):
-    """Assemble row-major packed C from equal column shards.
+                   group=None, widths: Optional[List[int]] = None, bits: int = 16,
+                   block: int = 128):
+    """Assemble row-major packed C from column shards.
 
     Each rank holds C[:, n0:n1] packed row-major ([M, nl] codes as storage
     words, [M, nl/block] scales).  Because every shard width is a whole
     number of scale blocks, row m of C is the concatenation over ranks of
-    their row m: gather [G, M, ...] and reorder to [M, G, ...].
+    their row m: gather [G, M, ...] and reorder to [M, G, ...].  ``widths``
+    (columns per rank) may differ by whole blocks; shards are then padded to
+    the widest for the gather.
     """
-    gp = _all_gather(c_packed.contiguous(), world, group)
-    gs = _all_gather(c_scales.contiguous(), world, group)
-    words = gp.view(world, M, -1).transpose(0, 1).reshape(-1)
-    scales = gs.view(world, M, -1).transpose(0, 1).reshape(-1)
-    return words, scales
+    if widths is None or len(set(widths)) == 1:
+        gp = _all_gather(c_packed.contiguous(), world, group)
+        gs = _all_gather(c_scales.contiguous(), world, group)
+        words = gp.view(world, M, -1).transpose(0, 1).reshape(-1)
+        scales = gs.view(world, M, -1).transpose(0, 1).reshape(-1)
+        return words, scales
+    per_word = 2 if bits == 16 else 8 // bits  # codes per storage element
+    words = _gather_rows_var(c_packed, M, world, [w // per_word for w in widths], group)
+    scales = _gather_rows_var(c_scales, M, world, [w // block for w in widths], group)
+    return words.reshape(-1), scales.reshape(-1)
 
 
 def sharded_quantize(x: torch.Tensor, dt, block: int, world: int, rank: int):

@@ -106,3 +106,125 @@ def test_row_sharded_quantize_concatenates_to_full():
         ss.append(s)
     assert np.array_equal(np.concatenate(ps), full_p)
     assert np.array_equal(np.concatenate(ss), full_s)
+
+
+# ── weight-only linear, column-sharded (configs[3] layout), uneven shards ──
+
+def _linear_inputs(dt_name, M=6, K=256, N=640):
+    g = torch.Generator().manual_seed(11)
+    w = torch.randn(N, K, generator=g) * 0.02
+    x = torch.randn(M, K, generator=g)
+    return x, w
+
+
+def _w_mx(dt_name, w, block=128):
+    """mx_linear's stored weight (W^T quantized flat) built with the oracle."""
+    from qtpytorch_b200.dtypes import get_mx_dtype
+    from qtpytorch_b200.hadamard import sign_vector
+    dt = get_mx_dtype(dt_name)
+    wt = w.t().contiguous().numpy()
+    signs = sign_vector(wt.shape[-1], dt.hadamard_seed).numpy() if dt.is_hadamard else None
+    p, s, n = O.quantize(wt, dt.bits, dt.kind, block, dt.is_hadamard, signs)
+    return mx_tensor(torch.from_numpy(p), torch.from_numpy(s), dt, wt.shape, n, block), signs
+
+
+def _shard_y(x, codes, scales, dt, K, nl, block):
+    """A rank's y[:, n0:n1] (oracle stand-in for the GPU kernel): float64
+    product of x and the shard's dequantized columns, rounded to fp32."""
+    wdq = O.dequant_flat(codes.numpy().reshape(-1), scales.numpy().reshape(-1), dt.bits,
+                         dt.kind, K * nl, block).reshape(K, nl)
+    return torch.from_numpy((x.numpy().astype(np.float64) @ wdq.astype(np.float64))
+                            .astype(np.float32))
+
+
+def _linear_rank(rank, port, dt_name, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        x, w = _linear_inputs(dt_name)
+        qw, signs = _w_mx(dt_name, w)
+        sw = P.ShardedLinearWeight(qw, WORLD, rank)
+        K, N = sw.K, sw.N
+        nl = sw.n1 - sw.n0
+        y_local = _shard_y(x, sw.codes, sw.scales, sw.dtype, K, nl, sw.block)
+        y = P.gather_dense_columns(y_local, x.shape[0], WORLD,
+                                   [b - a for a, b in sw.shards])
+        if sw.dtype.is_hadamard:
+            y = torch.from_numpy(O.unrotate(y.numpy(), signs))
+        if rank == 0:
+            result_q.put((y.numpy(), sw.shards))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("dt_name", ["int4d", "int2d", "int4dh"])
+def test_sharded_linear_uneven_shards_match_full(dt_name):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_linear_rank, args=(r, port, dt_name, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    y, shards = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert [(b - a) // 128 for a, b in shards] == [3, 2]  # 5 blocks over 2 ranks
+    # the full weight's columns, computed shard range by shard range
+    x, w = _linear_inputs(dt_name)
+    qw, signs = _w_mx(dt_name, w)
+    K, N = qw._mx_orig_shape
+    full = O.dequant_flat(qw._mx_packed.numpy(), qw._mx_scales.numpy(), qw._mx_dtype.bits,
+                          qw._mx_dtype.kind, K * N, 128).reshape(K, N)
+    parts = [(x.numpy().astype(np.float64) @ full[:, a:b].astype(np.float64)).astype(np.float32)
+             for a, b in shards]
+    ref = np.concatenate(parts, axis=1)
+    if qw._mx_dtype.is_hadamard:
+        ref = O.unrotate(ref, signs)
+    assert np.array_equal(y.view(np.uint32), ref.view(np.uint32))
+
+
+def _qgemm_uneven_rank(rank, port, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    try:
+        a, b = _inputs(M=32, K=256, N=640)
+        M, K = a.shape
+        N = b.shape[1]
+        pa, sa, _ = O.quantize(a.numpy(), 8, "int", 128)
+        pb, sb, _ = O.quantize(b.numpy(), 8, "int", 128)
+        qb = mx_tensor(torch.from_numpy(pb), torch.from_numpy(sb), int8d, (K, N), K * N, 128)
+        w = P.ShardedQGemmWeight(qb, WORLD, rank)
+        nl = w.n1 - w.n0
+        codes, cs, _ = O.qscale_matmul(O.unpack(pa, 8, M * K), sa, w.codes.numpy().reshape(-1),
+                                       w.scales.numpy().reshape(-1), M, K, nl, 128, 16)
+        words, scales = P.gather_columns(torch.from_numpy(O.pack(codes, 16)),
+                                         torch.from_numpy(cs), M, WORLD,
+                                         widths=[e - s for s, e in w.shards], bits=16,
+                                         block=128)
+        if rank == 0:
+            result_q.put((words.numpy(), scales.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_qgemm_uneven_shards():
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_qgemm_uneven_rank, args=(r, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    words, scales = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    a, b = _inputs(M=32, K=256, N=640)
+    M, K = a.shape
+    N = b.shape[1]
+    pa, sa, _ = O.quantize(a.numpy(), 8, "int", 128)
+    pb, sb, _ = O.quantize(b.numpy(), 8, "int", 128)
+    codes, cs, _ = O.qscale_matmul(O.unpack(pa, 8, M * K), sa, O.unpack(pb, 8, K * N), sb,
+                                   M, K, N, 128, 16)
+    assert np.array_equal(words, O.pack(codes, 16))
+    assert np.array_equal(scales.view(np.uint32), cs.view(np.uint32))

@@ -216,3 +216,22 @@ def test_decode_tc_uneven_k(M, dt):
     pw, sw, _ = O.quantize(w.t().contiguous().numpy(), d.bits, d.kind, 256)
     wdq = O.dequantize(pw, sw, d.bits, d.kind, (K, N), 256)
     _linear_check(y, x.float().numpy(), wdq)
+
+
+@pytest.mark.parametrize("dt", ["int4d", "int4dh"])
+def test_sharded_linear_single_rank_equals_module(dt):
+    """The column-sharded linear at world 1 runs the same kernel (and the
+    row unrotation for h dtypes) as mx_linear.forward."""
+    from qtpytorch_b200 import parallel as P
+    d = get_mx_dtype(dt)
+    g = torch.Generator().manual_seed(9)
+    lin = torch.nn.Linear(512, 640, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(640, 512, generator=g) * 0.02)
+    ml = mxb.mx_linear.from_linear(lin.cuda(), d, 128)
+    x = torch.randn(24, 512, generator=g).bfloat16().cuda()
+    sw = P.ShardedLinearWeight.from_module(ml, 1, 0)
+    y = P.sharded_linear(x, sw)
+    assert torch.equal(y, ml(x))
+    yb = P.sharded_linear(x, sw, out_dtype=torch.bfloat16)
+    assert yb.dtype == torch.bfloat16 and torch.equal(yb, ml(x).bfloat16())
