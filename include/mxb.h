@@ -140,6 +140,31 @@ int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
               float* c_scales, float* c_f32, void* workspace, size_t workspace_bytes,
               void* stream);
 
+/* Workspace bytes for mxb_qgemm_kmajor. */
+size_t mxb_qgemm_kmajor_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int block);
+
+/*
+ * The packed integer matmul in "k-major" mode: B quantized along K.  The
+ * reference's CPU matmul reads B's scales as b_scales viewed [K/block, N]
+ * (mxtorch.py:1354-1355) although `quantize` lays them along B's flat rows,
+ * so most elements of B meet another element's scale.  Here the caller
+ * passes B^T [N, K] quantized flat (`mx_tensor.quantize(B.t())`): with
+ * K % block == 0 every block is one column's K-block, its scale
+ * bt_scales[n * K/block + kb] is that of every element it covers, and
+ * C = sum_kb fl(fl(P * sa[m, kb]) * sb[n, kb]) is the quantized product
+ * dequant(A) @ dequant(B) up to fp32 rounding (1-bit codes count as +-1,
+ * their dequantized meaning; the reference's matmul sign-extends them to
+ * 0 / -1).  No counterpart in the reference; same arguments,
+ * requantization and result as mxb_qgemm otherwise.
+ *   bt_packed / bt_scales  B^T [N, K], bt_nscales = N * K / block
+ *   K % block == 0 and a_nscales == M * K / block, else MXB_E_SHAPE.
+ */
+int mxb_qgemm_kmajor(const void* a_packed, const float* a_scales, int64_t a_nscales,
+                     const void* bt_packed, const float* bt_scales, int64_t bt_nscales,
+                     int64_t M, int64_t K, int64_t N, int bits, int block, int out_bits,
+                     void* c_packed, float* c_scales, float* c_f32, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 /* Workspace bytes for mxb_linear_wonly. */
 size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits,
                                        int kind, int block, int mode);

@@ -13,6 +13,6 @@ from .dtypes import (  # noqa: F401
 from .dtypes import *  # noqa: F401,F403  (int4d, float4d, int8dh, ...)
 from .hadamard import sign_vector  # noqa: F401
 from .linear import mx_linear, to_mx  # noqa: F401
-from .tensor import mx_matmul, mx_tensor, register_kernel  # noqa: F401
+from .tensor import mx_matmul, mx_matmul_kmajor, mx_tensor, register_kernel  # noqa: F401
 
 __version__ = "0.1.0"

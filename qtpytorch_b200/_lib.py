@@ -48,6 +48,9 @@ PROTOTYPES = {
     "mxb_qgemm_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int]),
     "mxb_qgemm": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _int,
                          _vp, _vp, _vp, _vp, _sz, _vp]),
+    "mxb_qgemm_kmajor_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int]),
+    "mxb_qgemm_kmajor": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int,
+                                _int, _vp, _vp, _vp, _vp, _sz, _vp]),
     "mxb_linear_wonly_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int, _int]),
     "mxb_linear_wonly": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _i64, _int, _int, _int, _int,
                                 _vp, _vp, _sz, _vp]),

@@ -26,11 +26,25 @@ size_t mxb_qgemm_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int b
          align_up(mxb_requant_workspace_size(M * N, block));
 }
 
-int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
-              const void* b_packed, const float* b_scales, int64_t b_nscales, int64_t M,
-              int64_t K, int64_t N, int bits, int block, int out_bits, void* c_packed,
-              float* c_scales, float* c_f32, void* workspace, size_t workspace_bytes,
-              void* stream) {
+size_t mxb_qgemm_kmajor_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int block) {
+  if (M <= 0 || K <= 0 || N <= 0 || block <= 0) return 0;
+  // + the transposed scales + one byte per code of A and B (CUDA-core path)
+  return mxb_qgemm_workspace_size(M, K, N, bits, block) +
+         align_up((size_t)cdiv(K, block) * N * sizeof(float)) + align_up((size_t)M * K) +
+         align_up((size_t)K * N);
+}
+
+}  // extern "C"
+
+namespace {
+
+// One implementation for both B layouts.  b_kmajor: b is B^T [N, K]
+// quantized along K (K % block == 0), its scales s[n, kb].
+int qgemm_impl(const void* a_packed, const float* a_scales, int64_t a_nscales,
+               const void* b_packed, const float* b_scales, int64_t b_nscales, int64_t M,
+               int64_t K, int64_t N, int bits, int block, int out_bits, void* c_packed,
+               float* c_scales, float* c_f32, void* workspace, size_t workspace_bytes,
+               bool b_kmajor, void* stream) {
   if (!int_bits(bits) || !out_bits_ok(out_bits)) return MXB_E_DTYPE;
   if (M <= 0 || K <= 0 || N <= 0 || block <= 0) return MXB_E_SHAPE;
   if (M * K >= (int64_t)1 << 31 || K * N >= (int64_t)1 << 31 || M * N >= (int64_t)1 << 31)
@@ -39,30 +53,59 @@ int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
   if (out_bits == 32 ? c_f32 == nullptr : (!c_packed || !c_scales)) return MXB_E_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t kbn = cdiv(K, block);
-  const bool sa_ok = a_nscales == M * kbn;
-  const bool sb_ok = b_nscales == kbn * N;
   char* ws = static_cast<char*>(workspace);
   size_t left = workspace ? workspace_bytes : 0;
+  auto take = [&](size_t bytes) -> char* {
+    const size_t need = align_up(bytes);
+    if (left < need) return nullptr;
+    char* p = ws;
+    ws += need;
+    left -= need;
+    return p;
+  };
+  bool sa_ok = a_nscales == M * kbn;
+  bool sb_ok = b_nscales == kbn * N;
+  const float* sb = b_scales;
+  if (b_kmajor) {
+    if (K % block || !sa_ok || b_nscales != N * kbn) return MXB_E_SHAPE;
+    float* t = reinterpret_cast<float*>(take((size_t)kbn * N * sizeof(float)));
+    if (!t) return MXB_E_WORKSPACE;
+    int rc = transpose_scales(b_scales, kbn, N, t, st);
+    if (rc != MXB_OK) return rc;
+    sb = t;
+    sb_ok = true;
+  }
   const bool tc = tc_qgemm_eligible(M, K, N, bits, block, sa_ok, sb_ok, a_packed, b_packed, c_f32);
   // int16d output: the tcgen05 kernel requantizes in its epilogue
   const bool fused = tc && out_bits == 16 && ((uintptr_t)c_packed % 16) == 0;
   float* C = c_f32;
   if (C == nullptr && !fused) {
-    const size_t need = align_up((size_t)M * N * sizeof(float));
-    if (left < need) return MXB_E_WORKSPACE;
-    C = reinterpret_cast<float*>(ws);
-    ws += need;
-    left -= need;
+    C = reinterpret_cast<float*>(take((size_t)M * N * sizeof(float)));
+    if (!C) return MXB_E_WORKSPACE;
   }
   int rc;
   if (tc) {
     const size_t need = align_up(tc_qgemm_workspace(M, K, N, bits));
-    if (left < need) return MXB_E_WORKSPACE;
-    rc = tc_qgemm(a_packed, a_scales, b_packed, b_scales, M, K, N, bits, block, C,
+    char* w = need ? take(need) : ws;
+    if (need && !w) return MXB_E_WORKSPACE;
+    rc = tc_qgemm(a_packed, a_scales, b_packed, sb, M, K, N, bits, block, C,
                   fused ? static_cast<uint32_t*>(c_packed) : nullptr, fused ? c_scales : nullptr,
-                  ws, need, st);
-    ws += need;
-    left -= need;
+                  w, need, b_kmajor, st);
+  } else if (b_kmajor) {
+    // CUDA-core kernel: B row-major and both operands one byte per code
+    int8_t* b8 = reinterpret_cast<int8_t*>(take((size_t)K * N));
+    if (!b8) return MXB_E_WORKSPACE;
+    rc = widen_transpose(b_packed, K, N, bits, /*pm1*/ true, b8, st);
+    if (rc != MXB_OK) return rc;
+    const void* a8 = a_packed;
+    if (bits != 8) {
+      int8_t* w = reinterpret_cast<int8_t*>(take((size_t)M * K));
+      if (!w) return MXB_E_WORKSPACE;
+      rc = widen_codes(a_packed, M * K, bits, w, /*pm1*/ true, st);
+      if (rc != MXB_OK) return rc;
+      a8 = w;
+    }
+    rc = qgemm_generic(a8, a_scales, true, b8, sb, true, M, K, N, 8, block, C, st);
   } else {
     rc = qgemm_generic(a_packed, a_scales, sa_ok, b_packed, b_scales, sb_ok, M, K, N, bits,
                        block, C, st);
@@ -70,6 +113,30 @@ int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
   if (rc != MXB_OK || out_bits == 32 || fused) return rc;
   return mxb_requant_f32(C, M * N, block, out_bits, c_packed, c_scales, left ? ws : nullptr,
                          left, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int mxb_qgemm(const void* a_packed, const float* a_scales, int64_t a_nscales,
+              const void* b_packed, const float* b_scales, int64_t b_nscales, int64_t M,
+              int64_t K, int64_t N, int bits, int block, int out_bits, void* c_packed,
+              float* c_scales, float* c_f32, void* workspace, size_t workspace_bytes,
+              void* stream) {
+  return qgemm_impl(a_packed, a_scales, a_nscales, b_packed, b_scales, b_nscales, M, K, N, bits,
+                    block, out_bits, c_packed, c_scales, c_f32, workspace, workspace_bytes,
+                    false, stream);
+}
+
+int mxb_qgemm_kmajor(const void* a_packed, const float* a_scales, int64_t a_nscales,
+                     const void* bt_packed, const float* bt_scales, int64_t bt_nscales,
+                     int64_t M, int64_t K, int64_t N, int bits, int block, int out_bits,
+                     void* c_packed, float* c_scales, float* c_f32, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  return qgemm_impl(a_packed, a_scales, a_nscales, bt_packed, bt_scales, bt_nscales, M, K, N,
+                    bits, block, out_bits, c_packed, c_scales, c_f32, workspace,
+                    workspace_bytes, true, stream);
 }
 
 size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int kind,

@@ -61,6 +61,9 @@ struct Bars {
 static_assert(sizeof(Bars) <= kBarsBytes, "barrier block overflows its shared-memory slot");
 static_assert(offsetof(Bars, sbw) % 16 == 0, "float4 reads of sbw need 16-byte alignment");
 
+// B_KMAJOR: B is given as B^T [N, K] (each column's K run contiguous: the
+// layout of a matrix quantized along K) and read as a K-major operand.
+template <bool B_KMAJOR>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const float* __restrict__ sa,
@@ -109,12 +112,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (round > 0 && !mbar_wait(&bars->empty[s], (round - 1) & 1, kErrTimeoutEmpty)) break;
         mbar_expect_tx(&bars->full[s], kTileA + kTileB);
         tma_load_2d(sA + s * kTileA, &tmap_a, &bars->full[s], kb * BKB, m0);
-        tma_load_2d(sB + s * kTileB, &tmap_b, &bars->full[s], n0, kb * BKB);
+        if (B_KMAJOR)
+          tma_load_2d(sB + s * kTileB, &tmap_b, &bars->full[s], kb * BKB, n0);
+        else
+          tma_load_2d(sB + s * kTileB, &tmap_b, &bars->full[s], n0, kb * BKB);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(/*S32*/ 2, /*s8*/ 1, 0, /*B N-major*/ 1, BM, BN);
+      constexpr uint32_t idesc =
+          make_idesc(/*S32*/ 2, /*s8*/ 1, 0, /*B N-major*/ B_KMAJOR ? 0 : 1, BM, BN);
       for (int kb = 0; kb < kbn; ++kb) {
         const int s = kb % STAGES, round = kb / STAGES;
         const int b = kb & 1, use = kb >> 1;
@@ -124,8 +131,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a0 = smem_u32(sA + s * kTileA), b0 = smem_u32(sB + s * kTileB);
 #pragma unroll
         for (int kk = 0; kk < BKB / 32; ++kk) {
-          mma_i8(tbase + b * BN, desc_kmajor_sw128(a0 + kk * 32),
-                 desc_mnmajor_sw128(b0 + kk * 32 * BN, kTileB), idesc, kk > 0 ? 1u : 0u);
+          const uint64_t bd = B_KMAJOR ? desc_kmajor_sw128(b0 + kk * 32)
+                                       : desc_mnmajor_sw128(b0 + kk * 32 * BN, kTileB);
+          mma_i8(tbase + b * BN, desc_kmajor_sw128(a0 + kk * 32), bd, idesc, kk > 0 ? 1u : 0u);
         }
         mma_commit(&bars->empty[s]);
         mma_commit(&bars->tfull[b]);
@@ -241,10 +249,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Integer value of a raw code.  The reference's matmul sign-extends every
+// width, so a 1-bit code is 0 or -1 there; `pm1` gives 1-bit codes their
+// dequantized meaning instead (raw 0 -> +1, raw 1 -> -1), for the k-major
+// matmul whose result is the quantized product.
+template <int BITS>
+__device__ __forceinline__ int8_t code_value(uint32_t raw, bool pm1) {
+  if (BITS == 1 && pm1) return (raw & 1u) ? (int8_t)-1 : (int8_t)1;
+  return (int8_t)sext(raw, BITS);
+}
+
+// Scales of a matrix quantized along K (B^T [N, K], K % block == 0:
+// s[n, kb]) -> the [K/block, N] layout the GEMM kernels read.
+__global__ void __launch_bounds__(256) transpose_scales_kernel(const float* __restrict__ s,
+                                                               int kbn, int N,
+                                                               float* __restrict__ out) {
+  const int64_t total = (int64_t)kbn * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t kb = i / N, n = i % N;
+    out[i] = s[n * kbn + kb];
+  }
+}
+
+// B^T [N, K] packed codes -> B [K, N] one signed byte per code (for the
+// CUDA-core kernel, which reads B row-major).
+template <int BITS>
+__global__ void __launch_bounds__(256) widen_transpose_kernel(const uint8_t* __restrict__ bt,
+                                                              int K, int N, bool pm1,
+                                                              int8_t* __restrict__ out) {
+  constexpr int PER = 8 / BITS;
+  const int64_t total = (int64_t)K * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = i / N, n = i % N, e = n * K + k;
+    const uint32_t raw = (bt[e / PER] >> ((e % PER) * BITS)) & ((1u << BITS) - 1u);
+    out[i] = code_value<BITS>(raw, pm1);
+  }
+}
+
 // Widen packed sub-byte codes to one signed byte per code.
 template <int BITS>
 __global__ void __launch_bounds__(256) widen_codes_kernel(const uint8_t* __restrict__ p,
-                                                          int64_t n, int8_t* __restrict__ out) {
+                                                          int64_t n, bool pm1,
+                                                          int8_t* __restrict__ out) {
   constexpr int PER = 8 / BITS;
   const int64_t nbytes = (n + PER - 1) / PER;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nbytes;
@@ -253,20 +301,48 @@ __global__ void __launch_bounds__(256) widen_codes_kernel(const uint8_t* __restr
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
       const int64_t e = i * PER + j;
-      if (e < n) out[e] = (int8_t)sext((b >> (j * BITS)) & ((1u << BITS) - 1u), BITS);
+      if (e < n) out[e] = code_value<BITS>((b >> (j * BITS)) & ((1u << BITS) - 1u), pm1);
     }
   }
 }
 
-int widen(const void* p, int64_t n, int bits, int8_t* out, cudaStream_t st) {
+}  // namespace
+
+int transpose_scales(const float* s, int64_t kbn, int64_t N, float* out, cudaStream_t st) {
+  int64_t g = cdiv(kbn * N, 256);
+  if (g > kSMs * 8) g = kSMs * 8;
+  transpose_scales_kernel<<<(unsigned)g, 256, 0, st>>>(s, (int)kbn, (int)N, out);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+int widen_transpose(const void* bt, int64_t K, int64_t N, int bits, bool pm1, int8_t* out,
+                    cudaStream_t st) {
+  int64_t g = cdiv(K * N, 256);
+  if (g > kSMs * 16) g = kSMs * 16;
+  const uint8_t* p = static_cast<const uint8_t*>(bt);
+  switch (bits) {
+    case 1: widen_transpose_kernel<1><<<(unsigned)g, 256, 0, st>>>(p, (int)K, (int)N, pm1, out); break;
+    case 2: widen_transpose_kernel<2><<<(unsigned)g, 256, 0, st>>>(p, (int)K, (int)N, pm1, out); break;
+    case 4: widen_transpose_kernel<4><<<(unsigned)g, 256, 0, st>>>(p, (int)K, (int)N, pm1, out); break;
+    case 8: widen_transpose_kernel<8><<<(unsigned)g, 256, 0, st>>>(p, (int)K, (int)N, pm1, out); break;
+    default: return MXB_E_DTYPE;
+  }
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+namespace {
+
+int widen(const void* p, int64_t n, int bits, int8_t* out, cudaStream_t st, bool pm1 = false) {
   const int per = 8 / bits;
   int64_t g = cdiv(cdiv(n, per), 256);
   if (g > kSMs * 16) g = kSMs * 16;
   const uint8_t* src = static_cast<const uint8_t*>(p);
   switch (bits) {
-    case 1: widen_codes_kernel<1><<<(unsigned)g, 256, 0, st>>>(src, n, out); break;
-    case 2: widen_codes_kernel<2><<<(unsigned)g, 256, 0, st>>>(src, n, out); break;
-    case 4: widen_codes_kernel<4><<<(unsigned)g, 256, 0, st>>>(src, n, out); break;
+    case 1: widen_codes_kernel<1><<<(unsigned)g, 256, 0, st>>>(src, n, pm1, out); break;
+    case 2: widen_codes_kernel<2><<<(unsigned)g, 256, 0, st>>>(src, n, pm1, out); break;
+    case 4: widen_codes_kernel<4><<<(unsigned)g, 256, 0, st>>>(src, n, pm1, out); break;
     default: return MXB_E_DTYPE;
   }
   MXB_LAUNCH_CHECK();
@@ -293,6 +369,11 @@ EncodeTiledFn encode_fn() {
 }
 
 }  // namespace
+
+int widen_codes(const void* p, int64_t n, int bits, int8_t* out, bool pm1, cudaStream_t st) {
+  return widen(p, n, bits, out, st, pm1);
+}
+
 
 // 2-D row-major byte matrix [rows][cols] -> tensor map with a 128x128-byte box,
 // 128-byte swizzle.
@@ -335,8 +416,7 @@ size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits) {
 
 int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
              int64_t K, int64_t N, int bits, int block, float* C, uint32_t* q_words,
-             float* q_scales, void* ws, size_t wsb,
-             cudaStream_t st) {
+             float* q_scales, void* ws, size_t wsb, bool b_kmajor, cudaStream_t st) {
   (void)block;
   const void* a8 = a;
   const void* b8 = b;
@@ -344,22 +424,26 @@ int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int
     if (wsb < tc_qgemm_workspace(M, K, N, bits)) return MXB_E_WORKSPACE;
     int8_t* wa = static_cast<int8_t*>(ws);
     int8_t* wb = wa + (M * K + 255) / 256 * 256;
-    int rc = widen(a, M * K, bits, wa, st);
+    int rc = widen(a, M * K, bits, wa, st, b_kmajor);
     if (rc != MXB_OK) return rc;
-    rc = widen(b, K * N, bits, wb, st);
+    rc = widen(b, K * N, bits, wb, st, b_kmajor);
     if (rc != MXB_OK) return rc;
     a8 = wa;
     b8 = wb;
   }
   CUtensorMap ta, tb;
   if (make_tmap_u8(&ta, a8, (uint64_t)K, (uint64_t)M, BKB, BM) != MXB_OK) return MXB_E_CUDA;
-  if (make_tmap_u8(&tb, b8, (uint64_t)N, (uint64_t)K, BN, BKB) != MXB_OK) return MXB_E_CUDA;
+  if (b_kmajor ? make_tmap_u8(&tb, b8, (uint64_t)K, (uint64_t)N, BKB, BN)
+               : make_tmap_u8(&tb, b8, (uint64_t)N, (uint64_t)K, BN, BKB)) {
+    return MXB_E_CUDA;
+  }
+  auto kern = b_kmajor ? qgemm_tc_kernel<true> : qgemm_tc_kernel<false>;
   // set per call: the attribute belongs to the current device's context
-  MXB_CUDA_TRY(cudaFuncSetAttribute(qgemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
   dim3 grid((unsigned)(N / BN), (unsigned)(M / BM));
-  qgemm_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C,
-                                                      q_words, q_scales);
+  kern<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C, q_words,
+                                           q_scales);
   MXB_LAUNCH_CHECK();
   return MXB_OK;
 }

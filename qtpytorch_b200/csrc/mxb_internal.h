@@ -46,8 +46,14 @@ bool tc_qgemm_eligible(int64_t M, int64_t K, int64_t N, int bits, int block, boo
 size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits);
 int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
              int64_t K, int64_t N, int bits, int block, float* C, uint32_t* q_words,
-             float* q_scales, void* ws, size_t wsb,
-             cudaStream_t st);
+             float* q_scales, void* ws, size_t wsb, bool b_kmajor, cudaStream_t st);
+// (b_kmajor also gives 1-bit codes their +-1 meaning)
+// layout helpers of the k-major matmul
+int transpose_scales(const float* s, int64_t kbn, int64_t N, float* out, cudaStream_t st);
+// pm1: 1-bit codes as +-1 (their dequantized meaning) instead of 0 / -1
+int widen_transpose(const void* bt, int64_t K, int64_t N, int bits, bool pm1, int8_t* out,
+                    cudaStream_t st);
+int widen_codes(const void* p, int64_t n, int bits, int8_t* out, bool pm1, cudaStream_t st);
 bool tc_wonly_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
                        int64_t N, int bits, int kind, int block, const float* y);
 int tc_wonly(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,

@@ -129,11 +129,13 @@ def hadamard_rows(y: torch.Tensor, seed: int, inverse: bool) -> torch.Tensor:
 
 
 def qgemm(a_packed, a_scales, b_packed, b_scales, M: int, K: int, N: int, bits: int,
-          block: int, out_bits: int, want_f32: bool = False):
+          block: int, out_bits: int, want_f32: bool = False, b_kmajor: bool = False):
     """Packed integer matmul (mxtorch.py:5497-5573 CPU branch, bit-exact).
 
     Returns (c_packed, c_scales, c_f32 or None); c_packed is int32 words for
-    16-bit codes, int8 bytes otherwise.
+    16-bit codes, int8 bytes otherwise.  ``b_kmajor``: b_packed / b_scales
+    hold B^T [N, K] quantized along K (each element with its own block's
+    scale), computed by ``mxb_qgemm_kmajor``.
     """
     L.require_cuda(a_packed, "qgemm")
     dev = a_packed.device
@@ -146,16 +148,19 @@ def qgemm(a_packed, a_scales, b_packed, b_scales, M: int, K: int, N: int, bits: 
         c_packed = torch.empty(nbytes, dtype=torch.int8, device=dev)
     c_scales = torch.empty(nb, dtype=torch.float32, device=dev)
     c_f32 = torch.empty(M, N, dtype=torch.float32, device=dev) if want_f32 else None
-    wsb = lib.mxb_qgemm_workspace_size(M, K, N, bits, block)
+    wsf = lib.mxb_qgemm_kmajor_workspace_size if b_kmajor else lib.mxb_qgemm_workspace_size
+    fn = lib.mxb_qgemm_kmajor if b_kmajor else lib.mxb_qgemm
+    wsb = wsf(M, K, N, bits, block)
     ws = L.workspace(wsb, dev)
     a_packed, b_packed = a_packed.contiguous(), b_packed.to(dev).contiguous()
     a_scales, b_scales = a_scales.contiguous(), b_scales.to(dev).contiguous()
     with torch.cuda.device(dev):
-        rc = lib.mxb_qgemm(L.ptr(a_packed), L.ptr(a_scales), a_scales.numel(),
-                           L.ptr(b_packed), L.ptr(b_scales), b_scales.numel(), M, K, N, bits,
-                           block, out_bits, L.ptr(c_packed), L.ptr(c_scales), L.ptr(c_f32),
-                           L.ptr(ws), wsb, L.stream_of(dev))
-    L.check(rc, f"mxb_qgemm({M}x{K}x{N}, bits={bits})")
+        rc = fn(L.ptr(a_packed), L.ptr(a_scales), a_scales.numel(),
+                L.ptr(b_packed), L.ptr(b_scales), b_scales.numel(), M, K, N, bits,
+                block, out_bits, L.ptr(c_packed), L.ptr(c_scales), L.ptr(c_f32),
+                L.ptr(ws), wsb, L.stream_of(dev))
+    name = "mxb_qgemm_kmajor" if b_kmajor else "mxb_qgemm"
+    L.check(rc, f"{name}({M}x{K}x{N}, bits={bits})")
     return c_packed, c_scales, c_f32
 
 

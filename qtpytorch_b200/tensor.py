@@ -272,6 +272,38 @@ def _dispatch_qgemm(a: mx_tensor, b: mx_tensor, out_dt: mx_dtype) -> mx_tensor:
     return mx_tensor(c_packed, c_scales, out_dt, torch.Size([M, N]), M * N, block)
 
 
+def mx_matmul_kmajor(a, b, dtype="int8d", block: int = 128) -> mx_tensor:
+    """A @ B with B quantized along K (the k-major mode of the packed matmul).
+
+    ``a`` is an mx_tensor [M, K] or a float tensor (quantized with ``dtype``);
+    ``b`` is either a float B [K, N], quantized here as ``B.t()`` so every
+    block is one column's K-block, or an mx_tensor already holding B^T
+    [N, K].  Each element of B then meets its own block's scale, unlike the
+    reference's ``a @ b`` (whose B-scale view, mxtorch.py:1354-1355, pairs
+    most elements with another element's scale).  Needs K % block == 0.
+    The result is requantized like ``a @ b`` (int16d for int8 x int8)."""
+    dt = get_mx_dtype(dtype)
+    if not isinstance(a, mx_tensor):
+        a = mx_tensor.quantize(a.float(), dt, block)
+    if not isinstance(b, mx_tensor):
+        b = mx_tensor.quantize(b.float().t().contiguous(), a._mx_dtype, a._mx_block)
+    M, K = a._mx_orig_shape
+    N, K2 = b._mx_orig_shape
+    if K != K2:
+        raise ValueError(f"GEMM shape mismatch: {tuple(a._mx_orig_shape)} @ "
+                         f"B^T {tuple(b._mx_orig_shape)}")
+    if (a._mx_dtype.bits != b._mx_dtype.bits or a._mx_block != b._mx_block
+            or not (a._mx_dtype.is_int and b._mx_dtype.is_int)
+            or a._mx_dtype.variant != "" or b._mx_dtype.variant != ""
+            or a._mx_dtype.bits not in (1, 2, 4, 8)):
+        raise NotImplementedError("k-major matmul takes two base int dtypes of one width")
+    out_dt = optimal_output_dtype("matmul", a._mx_dtype, b._mx_dtype)
+    c_packed, c_scales, _ = ops.qgemm(a._mx_packed, a._mx_scales, b._mx_packed, b._mx_scales,
+                                      M, K, N, a._mx_dtype.bits, a._mx_block, out_dt.bits,
+                                      b_kmajor=True)
+    return mx_tensor(c_packed, c_scales, out_dt, torch.Size([M, N]), M * N, a._mx_block)
+
+
 def mx_matmul(a: torch.Tensor, b: torch.Tensor, dtype="int4d", block: int = 128) -> mx_tensor:
     """Quantize float operands if needed, then packed matmul (mxtorch.py:10694-10723)."""
     dt = get_mx_dtype(dtype)

@@ -235,3 +235,54 @@ def test_sharded_linear_single_rank_equals_module(dt):
     assert torch.equal(y, ml(x))
     yb = P.sharded_linear(x, sw, out_dtype=torch.bfloat16)
     assert yb.dtype == torch.bfloat16 and torch.equal(yb, ml(x).bfloat16())
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 384, 256), (40, 256, 96)])  # tcgen05 / CUDA-core
+@pytest.mark.parametrize("dt", ["int8d", "int4d", "int2d", "int1d"])
+def test_qgemm_kmajor(M, K, N, dt):
+    """k-major mode: B quantized along K (as B.t()).  Bit-exact against the
+    oracle's K-block formula fed B^T's codes and scales transposed into the
+    [K, N] / [K/block, N] layout, and within fp32 rounding of the fp64
+    dequant(A) @ dequant(B)."""
+    d = get_mx_dtype(dt)
+    g = torch.Generator().manual_seed(M + N + d.bits)
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(K, N, generator=g)
+    qa = mxb.mx_tensor.quantize(a.cuda(), d, 128)
+    qbt = mxb.mx_tensor.quantize(b.t().contiguous().cuda(), d, 128)
+    c = mxb.mx_matmul_kmajor(qa, qbt)
+    ob = c._mx_dtype.bits  # a.bits + b.bits snapped (int16d for int8 x int8)
+    c_packed, c_scales, c32 = ops.qgemm(qa._mx_packed, qa._mx_scales, qbt._mx_packed,
+                                        qbt._mx_scales, M, K, N, d.bits, 128, ob,
+                                        want_f32=True, b_kmajor=True)
+    assert L.load().mxb_device_error(1) == 0
+    kbn = K // 128
+    a_codes = O.unpack(qa._mx_packed.cpu().numpy(), d.bits, M * K)
+    bt_codes = O.unpack(qbt._mx_packed.cpu().numpy(), d.bits, N * K).reshape(N, K)
+    if d.bits == 1:  # k-major mode counts 1-bit codes as +-1 (their dequantized meaning)
+        a_codes = np.where(a_codes == 0, 1, -1).astype(a_codes.dtype)
+        bt_codes = np.where(bt_codes == 0, 1, -1).astype(bt_codes.dtype)
+    sbt = qbt._mx_scales.cpu().numpy().reshape(N, kbn)
+    codes, cs, C = O.qscale_matmul(a_codes, qa._mx_scales.cpu().numpy(),
+                                   np.ascontiguousarray(bt_codes.T).reshape(-1),
+                                   np.ascontiguousarray(sbt.T).reshape(-1), M, K, N, 128, ob)
+    assert np.array_equal(_u32(c32.cpu().numpy()), _u32(C))
+    want = O.pack(codes, ob)
+    assert np.array_equal(c_packed.cpu().numpy().view(want.dtype), want)
+    assert np.array_equal(_u32(c_scales.cpu().numpy()), _u32(cs))
+    assert np.array_equal(c._mx_packed.cpu().numpy(), c_packed.cpu().numpy())
+    # every element met its own scale: the fp64 quantized product
+    adq = O.dequant_flat(qa._mx_packed.cpu().numpy(), qa._mx_scales.cpu().numpy(), d.bits,
+                         d.kind, M * K, 128).reshape(M, K).astype(np.float64)
+    bdq = O.dequant_flat(qbt._mx_packed.cpu().numpy(), sbt.reshape(-1), d.bits, d.kind,
+                         N * K, 128).reshape(N, K).astype(np.float64).T
+    ref = adq @ bdq
+    bound = np.abs(adq) @ np.abs(bdq)
+    assert np.all(np.abs(C.astype(np.float64) - ref) <= 1e-5 * bound + 1e-30)
+
+
+def test_qgemm_kmajor_rejects_straddling_blocks():
+    qa = mxb.mx_tensor.quantize(torch.randn(8, 200).cuda(), mxb.int8d, 128)
+    qbt = mxb.mx_tensor.quantize(torch.randn(16, 200).cuda(), mxb.int8d, 128)
+    with pytest.raises(L.MxbError):
+        mxb.mx_matmul_kmajor(qa, qbt)
