@@ -432,6 +432,30 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
         out[f"quantize_{dt}_fp32_2^{n.bit_length() - 1}"] = {
             "ms": t, "gbs": byts / t / 1e6, "hbm_frac": byts / t / 1e6 / hbm}
         del x
+    # configs[4] sweep (bounded): int2d / int1d / float4d, fp32 and bf16
+    # N(0,1) inputs of 2^26 elements (larger than L2), block 32 and 128,
+    # quantize then dequantize; GB/s = algorithmic bytes / device time
+    sweep = {}
+    n = 1 << 26
+    for in_dt in (torch.float32, torch.bfloat16):
+        x = torch.randn(n, device=dev).to(in_dt)
+        ib = 4 if in_dt == torch.float32 else 2
+        for dt in ("int2d", "int1d", "float4d", "int4d", "int8d"):
+            d = mxb.get_mx_dtype(dt)
+            for blk in ((32, 128) if dt in ("int2d", "int1d", "float4d") else (128,)):
+                p_, s_, _ = ops.quantize(x, d, blk)
+                fq = graphed(lambda: ops.quantize(x, d, blk), stream)
+                tq = statistics.median(time_steps(fq, steps, flush, stream))
+                fd = graphed(lambda: ops.dequantize(p_, s_, d, n, blk), stream)
+                td = statistics.median(time_steps(fd, steps, flush, stream))
+                qb = n * ib + n * d.bits / 8 + n / blk * 4
+                db = n * d.bits / 8 + n / blk * 4 + n * 4
+                key = f"{dt}_{'fp32' if ib == 4 else 'bf16'}_b{blk}"
+                sweep[key] = {"q_gbs": round(qb / tq / 1e6, 1), "q_frac": round(qb / tq / 1e6 / hbm, 3),
+                              "dq_gbs": round(db / td / 1e6, 1), "dq_frac": round(db / td / 1e6 / hbm, 3)}
+                del p_, s_
+        del x
+    out["quant_dequant_sweep_2^26"] = sweep
     # configs[3] on one rank: int4dh weight-only linear, W 8192 x 8192 ~ N(0, 0.02)
     # with 8 outlier input channels x25, x bf16 [4096, 8192]; the sharded
     # linear at world 1 (GEMM + the 8192-point unrotation of y)

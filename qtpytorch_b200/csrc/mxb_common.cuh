@@ -54,7 +54,21 @@ __device__ __constant__ static const uint32_t kF4Grid[16] = {
     0xbdaaaaabu, 0x80000000u, 0x00000000u, 0x3daaaaabu, 0x3e2aaaabu, 0x3e800000u,
     0x3eaaaaabu, 0x3f000000u, 0x3f2aaaabu, 0x3f800000u};
 
-__device__ __forceinline__ float f4_grid(int idx) { return __uint_as_float(kF4Grid[idx & 15]); }
+// Grid value of a code without a memory lookup (lanes holding different
+// codes would serialise on the constant cache): index i < 8 is -mag[7 - i],
+// i >= 8 is +mag[i - 8], mag = {0, 1/12, 1/6, 1/4, 1/3, 1/2, 2/3, 1} as the
+// fp32 bit patterns of kF4Grid; a three-level select picks the magnitude.
+__device__ __forceinline__ float f4_grid(int idx) {
+  const int i = idx & 15;
+  const int j = i ^ (7 + (i >> 3));  // 7 - i below 8, i - 8 from 8
+  const uint32_t m01 = (j & 1) ? 0x3daaaaabu : 0x00000000u;  // 1/12 | 0
+  const uint32_t m23 = (j & 1) ? 0x3e800000u : 0x3e2aaaabu;  // 1/4 | 1/6
+  const uint32_t m45 = (j & 1) ? 0x3f000000u : 0x3eaaaaabu;  // 1/2 | 1/3
+  const uint32_t m67 = (j & 1) ? 0x3f800000u : 0x3f2aaaabu;  // 1 | 2/3
+  const uint32_t lo = (j & 2) ? m23 : m01, hi = (j & 2) ? m67 : m45;
+  const uint32_t mag = (j & 4) ? hi : lo;
+  return __uint_as_float(mag | ((i < 8) ? 0x80000000u : 0u));
+}
 
 // bucketize(v, mids, right=False) == number of boundaries strictly below v.
 // The 15 boundaries are symmetric: -p6..-p0, 0, p0..p6 with p = 1/24, 1/8,

@@ -218,45 +218,136 @@ __device__ __forceinline__ uint32_t raw_code(const uint8_t* __restrict__ packed,
   return (b >> ((e % PER) * BITS)) & ((1u << BITS) - 1u);
 }
 
+// 8 elements per lane and group (two float4 stores per lane), two groups
+// per iteration: cheaper per element where the decode itself is the cost.
+template <int BITS, int KIND>
+__device__ __forceinline__ void load_codes8(const uint8_t* __restrict__ packed, int64_t e0,
+                                            uint32_t (&w)[4]) {
+  const uint8_t* p = packed + (e0 * BITS) / 8;
+  if (BITS == 16) {
+    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(p));
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if (BITS == 8) {
+    const uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
+    w[0] = v.x; w[1] = v.y;
+  } else if (BITS == 4) {
+    w[0] = __ldcs(reinterpret_cast<const uint32_t*>(p));
+  } else if (BITS == 2) {
+    w[0] = __ldcs(reinterpret_cast<const uint16_t*>(p));
+  } else {
+    w[0] = *p;
+  }
+}
+
+template <int BITS, int KIND>
+__device__ __forceinline__ void dequant8_store(const uint32_t (&w)[4], float s, int64_t e0,
+                                               int64_t n, float* __restrict__ out) {
+  uint32_t c[8];
+  if (BITS == 8) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { c[i] = (w[0] >> (8 * i)) & 0xff; c[i + 4] = (w[1] >> (8 * i)) & 0xff; }
+  } else if (BITS == 16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { c[2 * i] = w[i] & 0xffff; c[2 * i + 1] = w[i] >> 16; }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = (w[0] >> (BITS * i)) & ((1u << BITS) - 1u);
+  }
+  float r[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) r[i] = dequant_code<BITS, KIND>(c[i], s);
+  if (e0 + 8 <= n) {
+    float4* o = reinterpret_cast<float4*>(out + e0);
+    __stcs(o, make_float4(r[0], r[1], r[2], r[3]));
+    __stcs(o + 1, make_float4(r[4], r[5], r[6], r[7]));
+  } else {
+    for (int i = 0; i < 8; ++i)
+      if (e0 + i < n) out[e0 + i] = r[i];
+  }
+}
+
+template <int BITS, int KIND>
+__global__ void __launch_bounds__(256) dequant_vec8_kernel(const uint8_t* __restrict__ packed,
+                                                           const float* __restrict__ scales,
+                                                           int64_t n, int block,
+                                                           float* __restrict__ out) {
+  const int64_t ngroups = (n + 7) / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ngroups; t += 2 * stride) {
+    const int64_t t2 = t + stride;
+    const bool two = t2 < ngroups;
+    uint32_t wa[4] = {0u, 0u, 0u, 0u}, wb[4] = {0u, 0u, 0u, 0u};
+    load_codes8<BITS, KIND>(packed, t * 8, wa);
+    const float sa = __ldg(scales + (t * 8) / block);
+    float sb = 0.0f;
+    if (two) {
+      load_codes8<BITS, KIND>(packed, t2 * 8, wb);
+      sb = __ldg(scales + (t2 * 8) / block);
+    }
+    dequant8_store<BITS, KIND>(wa, sa, t * 8, n, out);
+    if (two) dequant8_store<BITS, KIND>(wb, sb, t2 * 8, n, out);
+  }
+}
+
+// Codes of 4 consecutive elements starting at e0 (e0 % 4 == 0), low bits first.
+template <int BITS>
+__device__ __forceinline__ uint64_t load_codes4(const uint8_t* __restrict__ packed, int64_t e0) {
+  if (BITS == 16) {
+    const uint2 v = __ldcs(reinterpret_cast<const uint2*>(packed + e0 * 2));
+    return (uint64_t)v.x | ((uint64_t)v.y << 32);
+  } else if (BITS == 8) {
+    return __ldcs(reinterpret_cast<const uint32_t*>(packed + e0));
+  } else if (BITS == 4) {
+    return __ldcs(reinterpret_cast<const uint16_t*>(packed + e0 / 2));
+  } else if (BITS == 2) {
+    return __ldcs(packed + e0 / 4);
+  } else {
+    return (uint64_t)(__ldcs(packed + e0 / 8) >> (e0 & 4));
+  }
+}
+
+template <int BITS, int KIND>
+__device__ __forceinline__ void dequant4_store(uint64_t w, float s, int64_t e0, int64_t n,
+                                               float* __restrict__ out) {
+  float r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    r[i] = dequant_code<BITS, KIND>((uint32_t)(w >> (BITS * i)) & (uint32_t)((1ull << BITS) - 1u), s);
+  if (e0 + 4 <= n) {
+    __stcs(reinterpret_cast<float4*>(out + e0), make_float4(r[0], r[1], r[2], r[3]));
+  } else {
+    for (int i = 0; i < 4; ++i)
+      if (e0 + i < n) out[e0 + i] = r[i];
+  }
+}
+
+// 4 elements per lane and group, so each warp store covers 512 contiguous
+// bytes; four groups per iteration, all loads issued before any is used.
 template <int BITS, int KIND>
 __global__ void __launch_bounds__(256) dequant_vec_kernel(const uint8_t* __restrict__ packed,
                                                           const float* __restrict__ scales,
                                                           int64_t n, int block,
                                                           float* __restrict__ out) {
-  const int64_t ngroups = (n + 7) / 8;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ngroups;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t e0 = t * 8;
-    const float s = __ldg(scales + e0 / block);
-    uint32_t c[8];
-    const uint8_t* p = packed + (e0 * BITS) / 8;
-    if (BITS == 8) {
-      uint2 w = __ldcs(reinterpret_cast<const uint2*>(p));
+  constexpr int U = 4;
+  const int64_t ngroups = (n + 3) / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ngroups; t += U * stride) {
+    uint64_t w[U];
+    float sc[U];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) { c[i] = (w.x >> (8 * i)) & 0xff; c[i + 4] = (w.y >> (8 * i)) & 0xff; }
-    } else if (BITS == 16) {
-      uint4 w = __ldcs(reinterpret_cast<const uint4*>(p));
-      uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) { c[2 * i] = ws[i] & 0xffff; c[2 * i + 1] = ws[i] >> 16; }
-    } else {
-      uint32_t w;
-      if (BITS == 4) w = __ldcs(reinterpret_cast<const uint32_t*>(p));
-      else if (BITS == 2) w = __ldcs(reinterpret_cast<const uint16_t*>(p));
-      else w = *p;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) c[i] = (w >> (BITS * i)) & ((1u << BITS) - 1u);
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = t + u * stride;
+      w[u] = 0;
+      sc[u] = 0.0f;
+      if (g < ngroups) {
+        w[u] = load_codes4<BITS>(packed, g * 4);
+        sc[u] = __ldg(scales + (g * 4) / block);
+      }
     }
-    float r[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) r[i] = dequant_code<BITS, KIND>(c[i], s);
-    if (e0 + 8 <= n) {
-      float4* o = reinterpret_cast<float4*>(out + e0);
-      __stcs(o, make_float4(r[0], r[1], r[2], r[3]));
-      __stcs(o + 1, make_float4(r[4], r[5], r[6], r[7]));
-    } else {
-      for (int i = 0; i < 8; ++i)
-        if (e0 + i < n) out[e0 + i] = r[i];
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = t + u * stride;
+      if (g < ngroups) dequant4_store<BITS, KIND>(w[u], sc[u], g * 4, n, out);
     }
   }
 }
@@ -556,8 +647,25 @@ int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_
   }
   const size_t in_align = BITS == 16 ? 16 : (BITS == 8 ? 8 : (BITS == 4 ? 4 : (BITS == 2 ? 2 : 1)));
   if (block % 8 == 0 && aligned(packed, in_align) && aligned(out, 16)) {
-    dequant_vec_kernel<BITS, KIND><<<grid_for(cdiv(n, 8)), 256, 0, st>>>(packed, scales, n,
-                                                                         block, out);
+    // Measured at 2^26 elements (fraction of HBM copy bandwidth): the
+    // 4-element kernel reaches 0.75-0.79 for int2/int4/int8 (0.57-0.67 with
+    // 8 elements per lane); int1 (0.52 vs 0.47) and float4 (0.59 vs 0.49),
+    // where the decode costs more per element, keep the 8-element one.
+#ifndef MXB_DQ8_MASK
+#define MXB_DQ8_MASK 0x3  // bit 0: float4, bit 1: int1 take the 8-element kernel
+#endif
+    constexpr bool v8 = (KIND == MXB_KIND_FLOAT && (MXB_DQ8_MASK & 1)) ||
+                        (KIND == MXB_KIND_INT && BITS == 1 && (MXB_DQ8_MASK & 2)) ||
+                        (KIND == MXB_KIND_INT && BITS == 2 && (MXB_DQ8_MASK & 4)) ||
+                        (KIND == MXB_KIND_INT && BITS == 4 && (MXB_DQ8_MASK & 8)) ||
+                        (KIND == MXB_KIND_INT && BITS == 8 && (MXB_DQ8_MASK & 16)) ||
+                        (KIND == MXB_KIND_INT && BITS == 16 && (MXB_DQ8_MASK & 32));
+    if (v8)
+      dequant_vec8_kernel<BITS, KIND><<<grid_for(cdiv(n, 16)), 256, 0, st>>>(packed, scales, n,
+                                                                            block, out);
+    else
+      dequant_vec_kernel<BITS, KIND><<<grid_for(cdiv(n, 16)), 256, 0, st>>>(packed, scales, n,
+                                                                            block, out);
   } else {
     dequant_generic_kernel<BITS, KIND><<<grid_for(n), 256, 0, st>>>(packed, scales, n, block,
                                                                     out);
