@@ -2,8 +2,11 @@
 
 Headline: int8d x int8d packed GEMM, M=N=K=4096,
 block 128, seeded N(0,1) fp32 operands quantized on the device; output int16d
-(requantized, packed).  At N GPUs the weight B is column-sharded and the
-output all-gathered (strong scaling: the total work is fixed).
+(requantized, packed).  At N GPUs the weight B is column-sharded and every
+rank's GEMM epilogue writes its int16d tiles into all ranks' full outputs
+over NVLink (the all-gather fused into the kernel; `--gather nccl` times
+the NCCL all-gather + reorder instead).  Strong scaling: the total work is
+fixed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -232,7 +235,8 @@ def run_ours(args, world, rank, local):
     import qtpytorch_b200 as mxb
     from qtpytorch_b200 import _lib as L
     from qtpytorch_b200 import ops
-    from qtpytorch_b200.parallel import ShardedQGemmWeight, sharded_qgemm
+    from qtpytorch_b200.parallel import (PeerOutputs, ShardedQGemmWeight, sharded_qgemm,
+                                         sharded_qgemm_fused)
 
     dev = torch.device("cuda", local)
     lib = L.load()
@@ -251,8 +255,15 @@ def run_ours(args, world, rank, local):
     qb = mxb.mx_tensor.quantize(b_h.to(dev), mxb.int8d, BLOCK)
     w = ShardedQGemmWeight(qb, world, rank)
     nl = w.n1 - w.n0
+    # N > 1: each rank's GEMM epilogue writes its int16d tiles into every
+    # rank's full output over NVLink (CUDA IPC peer mappings), then one
+    # one-element all-reduce orders the ranks; no gather or reorder pass
+    fused = world > 1 and args.gather == "fused"
+    peers = PeerOutputs(M, N, BLOCK, world, rank, device=dev) if fused else None
 
     def step():
+        if fused:
+            return sharded_qgemm_fused(qa, w, peers)
         return sharded_qgemm(qa, w)
 
     # GEMM kernel alone (fp32 C, no requantization) for the roofline
@@ -321,7 +332,8 @@ def run_ours(args, world, rank, local):
         ea = mxb.mx_tensor.quantize(xa, mxb.int8d, BLOCK)
         torch.cuda.current_stream(dev).wait_stream(side)
         eb = mxb.mx_tensor.quantize(xb, mxb.int8d, BLOCK)
-        ec = sharded_qgemm(ea, ShardedQGemmWeight(eb, world, rank))
+        ew = ShardedQGemmWeight(eb, world, rank)
+        ec = sharded_qgemm_fused(ea, ew, peers) if fused else sharded_qgemm(ea, ew)
         out_words.copy_(ec._mx_packed, non_blocking=True)
         out_scales.copy_(ec._mx_scales, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
@@ -359,7 +371,10 @@ def run_ours(args, world, rank, local):
             "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "int8d x int8d GEMM M=N=K=4096 block 128 -> int16d "
                                    "(configs[1])",
-                       "global_batch": M, "parallelism": f"N-sharded x{world}",
+                       "global_batch": M,
+                       "parallelism": f"N-sharded x{world}" + (
+                           ", output gather fused into the GEMM epilogue (peer stores)"
+                           if fused else (", NCCL all-gather" if world > 1 else "")),
                        "l2": "flushed (256 MiB write) before every timed step"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak,
                          "unit": "TOPS", "frac": achieved / int8_peak, "traffic": traffic,
@@ -487,6 +502,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true")
+    ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
+                    help="N > 1: output gather fused into the GEMM kernel, or NCCL all-gather")
     ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant"],
                     help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()

@@ -165,6 +165,42 @@ int mxb_qgemm_kmajor(const void* a_packed, const float* a_scales, int64_t a_nsca
                      void* c_packed, float* c_scales, float* c_f32, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/*
+ * One rank's share of a column-sharded packed matmul with the output
+ * all-gather fused into the kernel.  The rank holds B's column shard
+ * [K, N_local] (its slice of the B-scale view, as mxb_qgemm reads it) and
+ * computes C[:, n_off : n_off + N_local] of the int16d result; the tcgen05
+ * epilogue writes each tile's packed codes and scale straight into the
+ * full-width outputs of all `nranks` ranks (this rank's own buffers and its
+ * peers' over NVLink, e.g. CUDA IPC mappings), rows of N_full columns, so
+ * no gather or reorder pass follows.  Output codes are int16d (the int8 x
+ * int8 result dtype; narrower operands give int16d here as well).  The
+ * caller makes the ranks' results visible to each other after the launch
+ * (a barrier on the stream, e.g. a one-element NCCL all-reduce) and must
+ * not let a rank write a buffer its peers are still reading (alternate two
+ * output sets).  No counterpart in the reference.
+ *   out_words[r]   rank r's M * N_full / 2 int32 words (16-byte aligned)
+ *   out_scales[r]  rank r's M * N_full / 128 floats
+ *   shapes: M, K, N_local multiples of 128, block 128, N_full % 128 == 0,
+ *   n_off % 128 == 0, 1 <= nranks <= 8; otherwise MXB_E_SHAPE / MXB_E_ARG.
+ *   Workspace: mxb_qgemm_workspace_size(M, K, N_local, bits, block).
+ */
+int mxb_qgemm_sharded(const void* a_packed, const float* a_scales, int64_t a_nscales,
+                      const void* b_packed, const float* b_scales, int64_t b_nscales,
+                      int64_t M, int64_t K, int64_t N_local, int bits, int block,
+                      int64_t N_full, int64_t n_off, int nranks, void* const* out_words,
+                      float* const* out_scales, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* Map a peer rank's device allocation into this process for the calling
+ * thread's current device (cudaIpcOpenMemHandle with lazy peer access):
+ * `handle` is the owner's cudaIpcMemHandle_t (handle_bytes == 64); *base
+ * receives the mapped base address.  Host plumbing for mxb_qgemm_sharded's
+ * output lists; no counterpart in the reference. */
+int mxb_ipc_open(const void* handle, int64_t handle_bytes, void** base);
+/* Unmap an address returned by mxb_ipc_open. */
+int mxb_ipc_close(void* base);
+
 /* Workspace bytes for mxb_linear_wonly. */
 size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits,
                                        int kind, int block, int mode);

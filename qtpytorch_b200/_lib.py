@@ -51,6 +51,10 @@ PROTOTYPES = {
     "mxb_qgemm_kmajor_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int]),
     "mxb_qgemm_kmajor": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int,
                                 _int, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "mxb_qgemm_sharded": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int,
+                                 _i64, _i64, _int, _vp, _vp, _vp, _sz, _vp]),
+    "mxb_ipc_open": (_int, [_vp, _i64, _vp]),
+    "mxb_ipc_close": (_int, [_vp]),
     "mxb_linear_wonly_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int, _int]),
     "mxb_linear_wonly": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _i64, _int, _int, _int, _int,
                                 _vp, _vp, _sz, _vp]),

@@ -88,9 +88,14 @@ int qgemm_impl(const void* a_packed, const float* a_scales, int64_t a_nscales,
     const size_t need = align_up(tc_qgemm_workspace(M, K, N, bits));
     char* w = need ? take(need) : ws;
     if (need && !w) return MXB_E_WORKSPACE;
-    rc = tc_qgemm(a_packed, a_scales, b_packed, sb, M, K, N, bits, block, C,
-                  fused ? static_cast<uint32_t*>(c_packed) : nullptr, fused ? c_scales : nullptr,
-                  w, need, b_kmajor, st);
+    QOut q{};
+    q.count = fused ? 1 : 0;
+    q.words[0] = static_cast<uint32_t*>(c_packed);
+    q.scales[0] = c_scales;
+    q.row_stride = (int)N;
+    q.col_off = 0;
+    rc = tc_qgemm(a_packed, a_scales, b_packed, sb, M, K, N, bits, block, C, &q, w, need,
+                  b_kmajor, st);
   } else if (b_kmajor) {
     // CUDA-core kernel: B row-major and both operands one byte per code
     int8_t* b8 = reinterpret_cast<int8_t*>(take((size_t)K * N));
@@ -137,6 +142,40 @@ int mxb_qgemm_kmajor(const void* a_packed, const float* a_scales, int64_t a_nsca
   return qgemm_impl(a_packed, a_scales, a_nscales, bt_packed, bt_scales, bt_nscales, M, K, N,
                     bits, block, out_bits, c_packed, c_scales, c_f32, workspace,
                     workspace_bytes, true, stream);
+}
+
+int mxb_qgemm_sharded(const void* a_packed, const float* a_scales, int64_t a_nscales,
+                      const void* b_packed, const float* b_scales, int64_t b_nscales,
+                      int64_t M, int64_t K, int64_t N_local, int bits, int block,
+                      int64_t N_full, int64_t n_off, int nranks, void* const* out_words,
+                      float* const* out_scales, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (!int_bits(bits)) return MXB_E_DTYPE;
+  if (M <= 0 || K <= 0 || N_local <= 0 || block <= 0) return MXB_E_SHAPE;
+  if (nranks < 1 || nranks > kMaxPeers || !out_words || !out_scales) return MXB_E_ARG;
+  if (N_full % 128 || n_off % 128 || n_off < 0 || n_off + N_local > N_full) return MXB_E_SHAPE;
+  if (M * K >= (int64_t)1 << 31 || K * N_local >= (int64_t)1 << 31 ||
+      M * N_full >= (int64_t)1 << 31)
+    return MXB_E_SHAPE;
+  if (!a_packed || !a_scales || !b_packed || !b_scales) return MXB_E_ARG;
+  const int64_t kbn = cdiv(K, block);
+  const bool sa_ok = a_nscales == M * kbn, sb_ok = b_nscales == kbn * N_local;
+  // the fused epilogue writes C only as int16d codes, so C itself is not needed
+  if (!tc_qgemm_eligible(M, K, N_local, bits, block, sa_ok, sb_ok, a_packed, b_packed, nullptr))
+    return MXB_E_SHAPE;
+  QOut q{};
+  q.count = nranks;
+  q.row_stride = (int)N_full;
+  q.col_off = (int)n_off;
+  for (int r = 0; r < nranks; ++r) {
+    if (!out_words[r] || !out_scales[r] || ((uintptr_t)out_words[r] & 15)) return MXB_E_ARG;
+    q.words[r] = static_cast<uint32_t*>(out_words[r]);
+    q.scales[r] = out_scales[r];
+  }
+  const size_t need = align_up(tc_qgemm_workspace(M, K, N_local, bits));
+  if (need && (!workspace || workspace_bytes < need)) return MXB_E_WORKSPACE;
+  return tc_qgemm(a_packed, a_scales, b_packed, b_scales, M, K, N_local, bits, block, nullptr,
+                  &q, workspace, need, false, static_cast<cudaStream_t>(stream));
 }
 
 size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int kind,

@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const float* __restrict__ sa,
                     const float* __restrict__ sb, int M, int N, int K, float* __restrict__ C,
-                    uint32_t* __restrict__ q_words, float* __restrict__ q_scales) {
+                    const __grid_constant__ QOut qout) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         out[c4] = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
     }
-    if (q_words != nullptr) {
+    if (qout.count > 0) {
       // Fused int16d requantization (mxtorch.py:1371-1378): the 128 columns
       // of this tile row are one scale block (N % 128 == 0, block 128).
       float a = 0.0f;
@@ -234,10 +234,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         w[c] = code[0] | (code[1] << 16);
       }
-      uint4* qo = reinterpret_cast<uint4*>(q_words + ((size_t)m * N + n0 + col0) / 2);
+      // The codes and scale go to every buffer of the list: this rank's
+      // output, or, for a column-sharded matmul, the full-width output of
+      // every rank (peer memory over NVLink) at this shard's column offset.
+      const size_t e = (size_t)m * qout.row_stride + qout.col_off + n0;
+      for (int r = 0; r < qout.count; ++r) {
+        uint4* qo = reinterpret_cast<uint4*>(qout.words[r] + (e + col0) / 2);
 #pragma unroll
-      for (int c = 0; c < kEpiCols / 8; ++c) qo[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-      if (ew < 4) q_scales[((size_t)m * N + n0) / BN] = cs;
+        for (int c = 0; c < kEpiCols / 8; ++c)
+          qo[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        if (ew < 4) qout.scales[r][e / BN] = cs;
+      }
+      if (qout.count > 1) __threadfence_system();
     }
   }
   __syncthreads();
@@ -415,8 +423,8 @@ size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits) {
 }
 
 int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
-             int64_t K, int64_t N, int bits, int block, float* C, uint32_t* q_words,
-             float* q_scales, void* ws, size_t wsb, bool b_kmajor, cudaStream_t st) {
+             int64_t K, int64_t N, int bits, int block, float* C, const QOut* qout, void* ws,
+             size_t wsb, bool b_kmajor, cudaStream_t st) {
   (void)block;
   const void* a8 = a;
   const void* b8 = b;
@@ -442,8 +450,9 @@ int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int
   MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)kSmemBytes));
   dim3 grid((unsigned)(N / BN), (unsigned)(M / BM));
-  kern<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C, q_words,
-                                           q_scales);
+  QOut none{};
+  kern<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C,
+                                           qout ? *qout : none);
   MXB_LAUNCH_CHECK();
   return MXB_OK;
 }

@@ -41,12 +41,24 @@ int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_
              float* y, float* partial, cudaStream_t st);
 
 // gemm_tc.cu (tcgen05)
+constexpr int kMaxPeers = 8;
+// int16d outputs of the int8 GEMM's fused requantization: `count` buffers
+// written with the same codes and scales (one for a plain matmul; every
+// rank's full-width output for a column-sharded one), rows of `row_stride`
+// columns, this launch's columns starting at `col_off`.
+struct QOut {
+  uint32_t* words[kMaxPeers];
+  float* scales[kMaxPeers];
+  int count;
+  int row_stride;
+  int col_off;
+};
 bool tc_qgemm_eligible(int64_t M, int64_t K, int64_t N, int bits, int block, bool sa_ok,
                        bool sb_ok, const void* a, const void* b, const float* c);
 size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits);
 int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int64_t M,
-             int64_t K, int64_t N, int bits, int block, float* C, uint32_t* q_words,
-             float* q_scales, void* ws, size_t wsb, bool b_kmajor, cudaStream_t st);
+             int64_t K, int64_t N, int bits, int block, float* C, const QOut* qout, void* ws,
+             size_t wsb, bool b_kmajor, cudaStream_t st);
 // (b_kmajor also gives 1-bit codes their +-1 meaning)
 // layout helpers of the k-major matmul
 int transpose_scales(const float* s, int64_t kbn, int64_t N, float* out, cudaStream_t st);

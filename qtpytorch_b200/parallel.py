@@ -90,6 +90,123 @@ def sharded_qgemm(qa: mx_tensor, w: ShardedQGemmWeight,
     return mx_tensor(words, scales, out_dt, torch.Size([M, w.N]), M * w.N, w.block)
 
 
+class PeerOutputs:
+    """Two sets of full-width int16d outputs (codes as int32 words, scales)
+    of a column-sharded matmul, each visible to every rank.
+
+    Every rank allocates its own buffers with torch; the CUDA IPC handles
+    (torch's tensor sharing) are exchanged on the host and each rank maps its
+    peers' buffers with its own device current (``mxb_ipc_open``): plain
+    peer mappings, no multicast object.  Calls alternate between the two
+    sets, so a rank that runs one call ahead never writes the set its peers
+    may still be reading."""
+
+    def __init__(self, M: int, N_full: int, block: int, world: int, rank: int, group=None,
+                 device=None):
+        from . import _lib as L
+        import ctypes as C
+        self.M, self.N, self.block, self.world, self.rank = M, N_full, block, world, rank
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        lib = L.load()
+        self._opened = []
+        self.sets = []
+        for _ in range(2):
+            words = torch.empty(M * N_full // 2, dtype=torch.int32, device=dev)
+            scales = torch.empty(M * N_full // block, dtype=torch.float32, device=dev)
+            mine = [self._share(t) for t in (words, scales)]
+            allh = [None] * world
+            if world > 1:
+                dist.all_gather_object(allh, mine, group=group)
+            else:
+                allh[0] = mine
+            ptr_w, ptr_s = [], []
+            for r in range(world):
+                if r == rank:
+                    ptr_w.append(words.data_ptr())
+                    ptr_s.append(scales.data_ptr())
+                    continue
+                got = []
+                for handle, off in allh[r]:
+                    base = C.c_void_p()
+                    with torch.cuda.device(dev):
+                        rc = lib.mxb_ipc_open(handle, len(handle), C.byref(base))
+                    L.check(rc, "mxb_ipc_open")
+                    self._opened.append(base.value)
+                    got.append(base.value + off)
+                ptr_w.append(got[0])
+                ptr_s.append(got[1])
+            self.sets.append({
+                "words": words, "scales": scales,
+                "ptr_w": (C.c_void_p * world)(*ptr_w), "ptr_s": (C.c_void_p * world)(*ptr_s)})
+        self.i = 0
+
+    @staticmethod
+    def _share(t: torch.Tensor):
+        """(cudaIpcMemHandle_t of t's CUDA allocation, byte offset of t in it).
+
+        torch's storage sharing returns its own handle encoding: a version
+        byte and a type byte ('c' for a cudaMalloc segment) before the
+        64-byte CUDA IPC handle; other types (expandable segments) cannot be
+        opened with cudaIpcOpenMemHandle and are refused."""
+        st = t.untyped_storage()
+        (_dev, handle, _size, storage_off, *_rest) = st._share_cuda_()
+        h = bytes(handle)
+        if len(h) == 66 and h[1] == ord("c"):
+            h = h[2:]
+        elif len(h) != 64:
+            raise RuntimeError(f"unsupported CUDA IPC handle encoding ({len(h)} bytes, "
+                               f"type {h[1:2]!r}); expandable segments cannot be mapped")
+        return h, int(storage_off) + t.storage_offset() * t.element_size()
+
+    def next(self):
+        s = self.sets[self.i]
+        self.i ^= 1
+        return s
+
+    def close(self):
+        from . import _lib as L
+        lib = L.load()
+        for b in self._opened:
+            lib.mxb_ipc_close(b)
+        self._opened = []
+
+
+def sharded_qgemm_fused(qa: mx_tensor, w: ShardedQGemmWeight, peers: PeerOutputs,
+                        group=None) -> mx_tensor:
+    """C = A @ B with B column-sharded, the output all-gather fused into the
+    GEMM kernel: every rank's epilogue writes its tiles' int16d codes and
+    scales straight into all ranks' full-width outputs (mxb_qgemm_sharded),
+    then a one-element all-reduce on the stream orders the ranks' writes
+    before any rank reads.  Same result as ``sharded_qgemm``; needs the
+    tcgen05 shapes (M, K and every shard a multiple of 128, block 128)."""
+    from . import _lib as L
+    import ctypes as C
+    M, K = qa._mx_orig_shape
+    if K != w.K:
+        raise ValueError("inner dimensions differ")
+    out_dt = optimal_output_dtype("matmul", qa._mx_dtype, w.dtype)
+    if out_dt.bits != 16:
+        raise NotImplementedError("the fused gather writes int16d codes (int8 x int8)")
+    nl = w.n1 - w.n0
+    dev = qa._mx_packed.device
+    lib = L.load()
+    wsb = lib.mxb_qgemm_workspace_size(M, K, nl, w.dtype.bits, w.block)
+    ws = L.workspace(wsb, dev)
+    out = peers.next()
+    with torch.cuda.device(dev):
+        rc = lib.mxb_qgemm_sharded(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales),
+                                   qa._mx_scales.numel(), L.ptr(w.codes), L.ptr(w.scales),
+                                   w.scales.numel(), M, K, nl, w.dtype.bits, w.block, w.N,
+                                   w.n0, w.world, C.cast(out["ptr_w"], C.c_void_p),
+                                   C.cast(out["ptr_s"], C.c_void_p), L.ptr(ws), wsb,
+                                   L.stream_of(dev))
+    L.check(rc, f"mxb_qgemm_sharded({M}x{K}x{nl} of {w.N})")
+    if w.world > 1:
+        flag = torch.zeros(1, device=dev)
+        dist.all_reduce(flag, group=group)  # every rank's kernel (and its peer stores) done
+    return mx_tensor(out["words"], out["scales"], out_dt, torch.Size([M, w.N]), M * w.N, w.block)
+
+
 class ShardedLinearWeight:
     """The column shard of an ``mx_linear`` weight (W^T [K, N] quantized flat,
     any code width) held by one rank: whole ``block``-column groups, so the
