@@ -45,6 +45,11 @@ constexpr int kTileB = BN * BKB;   // 16 KB
 constexpr int kTmemCols = 2 * BN;  // two int32 accumulators
 constexpr size_t kBarsBytes = 8192;  // >= sizeof(Bars), checked below
 constexpr size_t kSmemBytes = 1024 + (size_t)STAGES * (kTileA + kTileB) + kBarsBytes;
+// int16d codes of a tile staged row by row (BN / 2 words and a 16-byte pad
+// per row, so the lanes' 16-byte writes of 32 consecutive rows hit
+// different bank groups) in the TMA ring, idle once the last MMA is done
+constexpr int kStgRow = BN / 2 + 4;
+static_assert((size_t)BM * kStgRow * 4 <= (size_t)STAGES * kTileA, "staging fits the A ring");
 
 struct Bars {
   uint64_t full[STAGES];
@@ -57,6 +62,7 @@ struct Bars {
   alignas(16) float sbw[kEpiWarps][2 * kEpiCols];
   // per-row absmax of each 32-column slice, for the fused requantization
   float slice_amax[BN / kEpiCols][BM];
+  float row_scale[BM];  // the tile rows' int16d scales, staged for the copy-out
 };
 static_assert(sizeof(Bars) <= kBarsBytes, "barrier block overflows its shared-memory slot");
 static_assert(offsetof(Bars, sbw) % 16 == 0, "float4 reads of sbw need 16-byte alignment");
@@ -234,18 +240,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         w[c] = code[0] | (code[1] << 16);
       }
-      // The codes and scale go to every buffer of the list: this rank's
-      // output, or, for a column-sharded matmul, the full-width output of
-      // every rank (peer memory over NVLink) at this shard's column offset.
-      const size_t e = (size_t)m * qout.row_stride + qout.col_off + n0;
-      for (int r = 0; r < qout.count; ++r) {
-        uint4* qo = reinterpret_cast<uint4*>(qout.words[r] + (e + col0) / 2);
+      // Stage the tile's codes in shared memory, then send whole 256-byte
+      // rows with the bulk copy engine to every buffer of the list: this
+      // rank's output, or, for a column-sharded matmul, the full-width output
+      // of every rank (peer memory over NVLink) at this shard's column
+      // offset.  Whole rows keep NVLink packets full (one lane per row would
+      // send 16-byte pieces of 32 rows per store), and the copies do not hold
+      // the threads on remote latency.
+      uint32_t* stg = reinterpret_cast<uint32_t*>(sA);
 #pragma unroll
-        for (int c = 0; c < kEpiCols / 8; ++c)
-          qo[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-        if (ew < 4) qout.scales[r][e / BN] = cs;
+      for (int c = 0; c < kEpiCols / 8; ++c)
+        *reinterpret_cast<uint4*>(stg + row * kStgRow + col0 / 2 + 4 * c) =
+            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+      if (ew < 4) bars->row_scale[row] = cs;
+      fence_proxy_async_shared();
+      asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
+      const int te = threadIdx.x - 64;  // 0 .. 511
+      constexpr int kRowsPerLane = BM / (kEpiWarps * 2);  // 2 issuing lanes per warp
+      if (lane < 2) {
+        const int r0 = (ew * 2 + lane) * kRowsPerLane;
+        for (int r = 0; r < qout.count; ++r)
+          for (int rr = r0; rr < r0 + kRowsPerLane; ++rr) {
+            const size_t e = (size_t)(m0 + rr) * qout.row_stride + qout.col_off + n0;
+            bulk_store_s2g(qout.words[r] + e / 2, stg + rr * kStgRow, BN * 2);
+          }
+        bulk_commit();
       }
-      if (qout.count > 1) __threadfence_system();
+      if (te < BM) {
+        const size_t e = (size_t)(m0 + te) * qout.row_stride + qout.col_off + n0;
+        for (int r = 0; r < qout.count; ++r) qout.scales[r][e / BN] = bars->row_scale[te];
+      }
+      // The CTA waits only for its staging buffer to be read; the row copies
+      // (over NVLink for peers) finish while the next tiles compute, and are
+      // complete when the kernel is, which the caller's post-launch barrier
+      // orders before any rank reads.
+      if (lane < 2) bulk_wait_read();
     }
   }
   __syncthreads();
