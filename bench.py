@@ -259,7 +259,22 @@ def run_ours(args, world, rank, local):
     # rank's full output over NVLink (CUDA IPC peer mappings), then one
     # one-element all-reduce orders the ranks; no gather or reorder pass
     fused = world > 1 and args.gather == "fused"
-    peers = PeerOutputs(M, N, BLOCK, world, rank, device=dev) if fused else None
+    peers, fuse_note = None, None
+    if fused:
+        # all ranks map their peers' outputs; if any rank cannot, all use
+        # the NCCL all-gather instead (decided together, so none waits alone)
+        try:
+            peers = PeerOutputs(M, N, BLOCK, world, rank, device=dev)
+            ok = 1
+        except Exception as e:  # noqa: BLE001 - reported in the JSON line
+            fuse_note = f"peer mapping failed on rank {rank}: {e}"[:200]
+            ok = 0
+        import torch.distributed as dist
+        flag = torch.tensor([ok], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        if int(flag.item()) == 0:
+            fused = False
+            fuse_note = fuse_note or "a peer rank could not map the outputs"
 
     def step():
         if fused:
@@ -374,7 +389,8 @@ def run_ours(args, world, rank, local):
                        "global_batch": M,
                        "parallelism": f"N-sharded x{world}" + (
                            ", output gather fused into the GEMM epilogue (peer stores)"
-                           if fused else (", NCCL all-gather" if world > 1 else "")),
+                           if fused else (", NCCL all-gather" if world > 1 else "")
+                           + (f" ({fuse_note})" if fuse_note else "")),
                        "l2": "flushed (256 MiB write) before every timed step"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak,
                          "unit": "TOPS", "frac": achieved / int8_peak, "traffic": traffic,
