@@ -293,6 +293,10 @@ int launch_wide(int mt, int lb, dim3 grid, const XT* x, int M, int K, const uint
     if (mt == 1) return launch_wide_t<BITS, 16, 1, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
     return launch_wide_t<BITS, 16, 2, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
   }
+  if (lb == 8 && mt <= 2) {
+    if (mt == 1) return launch_wide_t<BITS, 8, 1, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
+    return launch_wide_t<BITS, 8, 2, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
+  }
   switch (mt) {
     case 4: return launch_wide_t<BITS, LBN, 4, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
     case 8: return launch_wide_t<BITS, LBN, 8, XT>(grid, x, M, K, W, ws, N, block, krows, part, st);
@@ -329,7 +333,10 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
   if (((uintptr_t)w % (uintptr_t)bits) || ((uintptr_t)y % 16)) return p;
   const int mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16;
   if (kind == MXB_KIND_INT && (bits == 4 || bits == 8)) {
-    const int lb = mt <= 2 ? 16 : (bits == 4 ? 4 : 8);
+    // M <= 2: int4 loads 8 bytes per lane and row (16 columns; fewer
+    // registers, more resident warps), int8 16 bytes -- each measured the
+    // faster of the two on configs[2]-sized weights
+    const int lb = mt <= 2 ? (bits == 4 ? 8 : 16) : (bits == 4 ? 4 : 8);
     const int cpt = wide_cpt(bits, lb);
     const int cols = 32 * cpt;
     if (N % cpt == 0 && block % cpt == 0 && ((uintptr_t)w % lb) == 0) {
