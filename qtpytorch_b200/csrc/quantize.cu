@@ -51,7 +51,12 @@ __device__ __forceinline__ uint32_t code_of(float v, float mul) {
   } else {
     const float m = (float)((1 << (BITS - 1)) - 1);
     float q = (MODE == Q_INT_RECIP) ? __fmul_rn(v, mul) : __fdiv_rn(v, mul);
-    q = nan_min(nan_max(q, -m), m);  // clamp; NaN stays NaN
+    // The reference clamps q to [-m, m] before rounding; here that clamp
+    // never changes a code, so it is left out.  Every |x| of a block is at
+    // most a = max(amax, 1e-12), and mul = fl(fl(1/a) * m) (or the divisor
+    // fl(a / m)), so |q| <= m (1 + 2^-24)^3 < m + 0.5, which rounds to m; a
+    // block whose amax is inf or NaN makes q 0 or NaN either way.
+    (void)m;
     // Round half to even by adding 1.5 * 2^23 (|q| <= 32767 < 2^22): the sum's
     // low mantissa bits are the two's-complement code.  NaN stores code 0, as
     // the reference's NaN -> int conversion does.
