@@ -42,7 +42,9 @@ __device__ __forceinline__ void block_factor(float amax, float& scale, float& mu
   }
 }
 
-template <int BITS, int MODE>
+// NAN_SELECT false: the caller has checked that the block's multiplier (or
+// divisor) is finite and positive, so no quotient is NaN (see quant8_store).
+template <int BITS, int MODE, bool NAN_SELECT = true>
 __device__ __forceinline__ uint32_t code_of(float v, float mul) {
   if (MODE == Q_FLOAT4) {
     return (uint32_t)f4_bucket(__fdiv_rn(v, mul));
@@ -61,7 +63,7 @@ __device__ __forceinline__ uint32_t code_of(float v, float mul) {
     // low mantissa bits are the two's-complement code.  NaN stores code 0, as
     // the reference's NaN -> int conversion does.
     const uint32_t c = __float_as_uint(__fadd_rn(q, 12582912.0f)) & ((1u << BITS) - 1u);
-    return q == q ? c : 0u;
+    return (!NAN_SELECT || q == q) ? c : 0u;
   }
 }
 
@@ -81,7 +83,15 @@ __device__ __forceinline__ void quant8_store(const float (&v)[8], bool valid, in
   if ((threadIdx.x & (L - 1)) == 0) scales[blk] = scale;
   uint32_t c[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = code_of<BITS, MODE>(v[i], mul);
+  for (int i = 0; i < 8; ++i) c[i] = code_of<BITS, MODE, MODE == Q_FLOAT4 || BITS == 1>(v[i], mul);
+  if (MODE != Q_FLOAT4 && BITS != 1 && !(mul > 0.0f && mul <= 3.4028235e38f)) {
+    // A NaN in the block makes amax and mul NaN, an inf makes the multiplier
+    // 0 (the divisor inf): every quotient is then 0 or NaN, and every code 0.
+    // A finite positive mul means every x of the block is finite, so no
+    // quotient is NaN and the per-element NaN test above is not needed.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = 0u;
+  }
   uint8_t* p = packed + (e0 * BITS) / 8;
   if (BITS == 8) {
     uint2 w;
