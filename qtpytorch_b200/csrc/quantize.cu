@@ -67,32 +67,37 @@ __device__ __forceinline__ uint32_t code_of(float v, float mul) {
   }
 }
 
-// Quantize 8 consecutive values owned by this lane; `L` lanes form a block.
-// Writes the packed codes of these 8 elements at byte offset (e0 * BITS / 8).
-template <int BITS, int MODE>
-__device__ __forceinline__ void quant8_store(const float (&v)[8], bool valid, int L,
+// Quantize E (8 or 16) consecutive values owned by this lane; `L` lanes form
+// a block.  Writes the packed codes of these elements at byte offset
+// (e0 * BITS / 8).  With 16 per lane the block's absmax shuffles and scale
+// computation are shared by twice as many elements.
+template <int BITS, int MODE, int E = 8>
+__device__ __forceinline__ void quant8_store(const float (&v)[E], bool valid, int L,
                                              int64_t e0, uint8_t* __restrict__ packed,
                                              float* __restrict__ scales, int64_t blk) {
   float a = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) a = amax_step(a, v[i]);
+  for (int i = 0; i < E; ++i) a = amax_step(a, v[i]);
   for (int o = L >> 1; o > 0; o >>= 1) a = nan_max(a, __shfl_xor_sync(0xffffffffu, a, o));
   if (!valid) return;
   float scale, mul;
   block_factor<BITS, MODE>(a, scale, mul);
   if ((threadIdx.x & (L - 1)) == 0) scales[blk] = scale;
-  uint32_t c[8];
+  uint32_t cc[E];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = code_of<BITS, MODE, MODE == Q_FLOAT4 || BITS == 1>(v[i], mul);
+  for (int i = 0; i < E; ++i) cc[i] = code_of<BITS, MODE, MODE == Q_FLOAT4 || BITS == 1>(v[i], mul);
   if (MODE != Q_FLOAT4 && BITS != 1 && !(mul > 0.0f && mul <= 3.4028235e38f)) {
     // A NaN in the block makes amax and mul NaN, an inf makes the multiplier
     // 0 (the divisor inf): every quotient is then 0 or NaN, and every code 0.
     // A finite positive mul means every x of the block is finite, so no
     // quotient is NaN and the per-element NaN test above is not needed.
 #pragma unroll
-    for (int i = 0; i < 8; ++i) c[i] = 0u;
+    for (int i = 0; i < E; ++i) cc[i] = 0u;
   }
-  uint8_t* p = packed + (e0 * BITS) / 8;
+#pragma unroll
+  for (int h = 0; h < E / 8; ++h) {
+  const uint32_t* c = cc + 8 * h;
+  uint8_t* p = packed + ((e0 + 8 * h) * BITS) / 8;
   if (BITS == 8) {
     uint2 w;
     w.x = c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24);
@@ -121,6 +126,7 @@ __device__ __forceinline__ void quant8_store(const float (&v)[8], bool valid, in
     for (int i = 0; i < 8; ++i) w |= c[i] << i;
     *p = (uint8_t)w;
   }
+  }
 }
 
 template <typename InT>
@@ -148,13 +154,14 @@ __device__ __forceinline__ void load8(const InT* __restrict__ x, int64_t e0, int
   }
 }
 
-// Vectorised quantize: block in {8,16,32,64,128,256}.
-template <typename InT, int BITS, int MODE>
+// Vectorised quantize: block in {8,16,32,64,128,256}; E elements per lane
+// (16 needs block % 16 == 0).
+template <typename InT, int BITS, int MODE, int E = 8>
 __global__ void __launch_bounds__(256) quant_vec_kernel(const InT* __restrict__ x, int64_t n,
                                                         int block, int64_t nb, bool vec,
                                                         uint8_t* __restrict__ packed,
                                                         float* __restrict__ scales) {
-  const int L = block / 8;
+  const int L = block / E;
   const int64_t groups = nb * (int64_t)L;  // threads with work
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -162,9 +169,11 @@ __global__ void __launch_bounds__(256) quant_vec_kernel(const InT* __restrict__ 
   for (int64_t w = warp0; w * 32 < groups; w += nwarps) {
     const int64_t t = w * 32 + lane;
     const bool valid = t < groups;
-    float v[8];
-    load8<InT>(x, t * 8, valid ? n : 0, vec, v);
-    quant8_store<BITS, MODE>(v, valid, L, t * 8, packed, scales, t / L);
+    float v[E];
+#pragma unroll
+    for (int h = 0; h < E / 8; ++h)
+      load8<InT>(x, t * E + 8 * h, valid ? n : 0, vec, *reinterpret_cast<float(*)[8]>(v + 8 * h));
+    quant8_store<BITS, MODE, E>(v, valid, L, t * E, packed, scales, t / L);
   }
 }
 
@@ -573,8 +582,15 @@ int quant_flat(const InT* x, int64_t n, int block, uint8_t* packed, float* scale
   const bool out_ok = aligned(packed, store_align < 1 ? 1 : store_align);
   if (vec_block(block) && out_ok) {
     const bool vec = aligned(x, 16);
-    quant_vec_kernel<InT, BITS, MODE><<<grid_for(nb * (block / 8)), 256, 0, st>>>(
-        x, n, block, nb, vec, packed, scales);
+    // 16 elements per lane where the block allows: the per-block shuffles
+    // and scale arithmetic are shared by twice the elements (measured at 2^26
+    // elements: int4d 0.77 -> 0.85 of HBM from fp32, 0.43 -> 0.56 from bf16)
+    if (block % 16 == 0)
+      quant_vec_kernel<InT, BITS, MODE, 16><<<grid_for(nb * (block / 16)), 256, 0, st>>>(
+          x, n, block, nb, vec, packed, scales);
+    else
+      quant_vec_kernel<InT, BITS, MODE><<<grid_for(nb * (block / 8)), 256, 0, st>>>(
+          x, n, block, nb, vec, packed, scales);
     MXB_LAUNCH_CHECK();
     return MXB_OK;
   }
