@@ -6,14 +6,16 @@
 // The scale varies along K, so it cannot move to the epilogue.  Instead the
 // dequantized weight w (exact fp32, the reference's value) is split into
 // bf16 planes: hi = bf16(w), mid = bf16(w - hi), |w - hi - mid| <= 2^-18 |w|.
-// Parity mode issues one kind::f16 MMA per plane (x is exact in bf16); fast
-// mode uses hi only.
+// Parity mode multiplies x (exact in bf16) by both planes with one
+// kind::f16 MMA of N = 256 per K slice (the planes are stored back to back
+// as one 256-row operand) into hi and mid partial sums that the epilogue
+// adds; fast mode uses hi only (N = 128).
 //
 // One CTA owns a 256 x 128 tile of y (two M=128 accumulators in TMEM that
 // share the weight planes):
 //   warp 0     TMA producer: x [256 x 64] bf16 (128-byte swizzle) and the
 //              packed codes [64 K rows x 128 N] per K step, 3-stage ring;
-//   warp 1     TMEM allocation and MMA issue (4 K=16 steps x 2 halves x planes);
+//   warp 1     TMEM allocation and MMA issue (4 K=16 steps x 2 halves);
 //   warps 2-9  transform, two groups of 4 taking alternate K steps (group j
 //              fills plane buffer j): each thread dequantizes an 8 (N) x 8 (K)
 //              unit of codes and writes the bf16 planes straight into the
@@ -35,7 +37,6 @@ constexpr int kAHalf = 128 * BK * 2;      // 16 KB
 constexpr int kAStage = 2 * kAHalf;       // 32 KB
 constexpr int kPlane = BN * BK * 2;       // 16 KB
 constexpr int kCodeStageMax = BK * BN;    // int8: 8 KB
-constexpr int kTmemCols = 2 * BN;         // two fp32 accumulators
 constexpr size_t kBarsBytes = 256;
 constexpr size_t kSmemBytes =
     1024 + (size_t)STAGES * kAStage + 2 * 2 * kPlane + (size_t)STAGES * kCodeStageMax + kBarsBytes;
@@ -94,6 +95,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int M, int N, int K, int block, float* __restrict__ y) {
   constexpr int kCodeRow = BN * BITS / 8;     // bytes of one K row of the code tile
   constexpr int kCodeStage = BK * kCodeRow;
+  // parity: per M half one N = 256 accumulator, columns [0, 128) the hi
+  // plane's products and [128, 256) the mid plane's (the planes are stored
+  // back to back, so they form one 256-row B operand: each x tile is read
+  // once per K slice instead of once per plane); fast: hi only
+  constexpr int kAcc = FAST ? BN : 2 * BN;
+  constexpr uint32_t kCols = 2 * kAcc;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -123,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmap_w);
   }
   if (warp == 1) {
-    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_alloc(&bars->tmem_base, kCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -144,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(/*F32*/ 1, /*BF16*/ 1, 0, 0, 128, BN);
+      constexpr uint32_t idesc = make_idesc(/*F32*/ 1, /*BF16*/ 1, 0, 0, 128, kAcc);
       for (int ks = 0; ks < ksteps; ++ks) {
         const int s = ks % STAGES, round = ks / STAGES;
         const int j = ks & 1, usej = ks >> 1;
@@ -153,15 +160,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a0 = smem_u32(sA + s * kAStage);
         const uint32_t phi = smem_u32(sP + (2 * j) * kPlane);
-        const uint32_t pmid = smem_u32(sP + (2 * j + 1) * kPlane);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint64_t ad = desc_kmajor_sw128(a0 + h * kAHalf + kk * 32);
-            mma_f16(tbase + h * BN, ad, desc_kmajor_sw128(phi + kk * 32), idesc,
+            mma_f16(tbase + h * kAcc, ad, desc_kmajor_sw128(phi + kk * 32), idesc,
                     (ks > 0 || kk > 0) ? 1u : 0u);
-            if (!FAST) mma_f16(tbase + h * BN, ad, desc_kmajor_sw128(pmid + kk * 32), idesc, 1u);
           }
         }
         mma_commit(&bars->empty[s]);
@@ -258,9 +263,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m = m0 + h * 128 + q * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + ((uint32_t)(q * 32) << 16) + h * BN + c * 32, r);
+          uint32_t r[32], rm[32];
+          const uint32_t ta = tbase + ((uint32_t)(q * 32) << 16) + h * kAcc + c * 32;
+          tmem_ld32(ta, r);
+          if (!FAST) tmem_ld32(ta + BN, rm);
           tmem_wait_ld();
+          if (!FAST) {
+#pragma unroll
+            for (int v = 0; v < 32; ++v)
+              r[v] = __float_as_uint(__fadd_rn(__uint_as_float(r[v]), __uint_as_float(rm[v])));
+          }
           if (m < M) {
             float4* o = reinterpret_cast<float4*>(y + (size_t)m * N + n0 + c * 32);
 #pragma unroll
@@ -278,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait(&bars->accfull, 0, kErrTimeoutDone);
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tbase, kTmemCols);
+    tmem_dealloc(tbase, kCols);
   }
 }
 
