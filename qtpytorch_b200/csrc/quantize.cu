@@ -263,9 +263,11 @@ __device__ __forceinline__ void load_codes8(const uint8_t* __restrict__ packed, 
   }
 }
 
+// tbl: the float4 grid in shared memory (float4 only; nullptr otherwise)
 template <int BITS, int KIND>
 __device__ __forceinline__ void dequant8_store(const uint32_t (&w)[4], float s, int64_t e0,
-                                               int64_t n, float* __restrict__ out) {
+                                               int64_t n, float* __restrict__ out,
+                                               const float* tbl = nullptr) {
   uint32_t c[8];
   if (BITS == 8) {
 #pragma unroll
@@ -279,7 +281,8 @@ __device__ __forceinline__ void dequant8_store(const uint32_t (&w)[4], float s, 
   }
   float r[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) r[i] = dequant_code<BITS, KIND>(c[i], s);
+  for (int i = 0; i < 8; ++i)
+    r[i] = KIND == MXB_KIND_FLOAT ? __fmul_rn(tbl[c[i] & 15u], s) : dequant_code<BITS, KIND>(c[i], s);
   if (e0 + 8 <= n) {
     float4* o = reinterpret_cast<float4*>(out + e0);
     __stcs(o, make_float4(r[0], r[1], r[2], r[3]));
@@ -295,6 +298,14 @@ __global__ void __launch_bounds__(256) dequant_vec8_kernel(const uint8_t* __rest
                                                            const float* __restrict__ scales,
                                                            int64_t n, int block,
                                                            float* __restrict__ out) {
+  // float4: the 16 grid values in shared memory, one bank each, so lanes
+  // reading different codes do not conflict (one load per value instead of
+  // a select chain)
+  __shared__ float tbl[16];
+  if (KIND == MXB_KIND_FLOAT) {
+    if (threadIdx.x < 16) tbl[threadIdx.x] = f4_grid((int)threadIdx.x);
+    __syncthreads();
+  }
   const int64_t ngroups = (n + 7) / 8;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ngroups; t += 2 * stride) {
@@ -308,8 +319,8 @@ __global__ void __launch_bounds__(256) dequant_vec8_kernel(const uint8_t* __rest
       load_codes8<BITS, KIND>(packed, t2 * 8, wb);
       sb = __ldg(scales + (t2 * 8) / block);
     }
-    dequant8_store<BITS, KIND>(wa, sa, t * 8, n, out);
-    if (two) dequant8_store<BITS, KIND>(wb, sb, t2 * 8, n, out);
+    dequant8_store<BITS, KIND>(wa, sa, t * 8, n, out, tbl);
+    if (two) dequant8_store<BITS, KIND>(wb, sb, t2 * 8, n, out, tbl);
   }
 }
 
@@ -332,11 +343,13 @@ __device__ __forceinline__ uint64_t load_codes4(const uint8_t* __restrict__ pack
 
 template <int BITS, int KIND>
 __device__ __forceinline__ void dequant4_store(uint64_t w, float s, int64_t e0, int64_t n,
-                                               float* __restrict__ out) {
+                                               float* __restrict__ out, const float* tbl) {
   float r[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    r[i] = dequant_code<BITS, KIND>((uint32_t)(w >> (BITS * i)) & (uint32_t)((1ull << BITS) - 1u), s);
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t raw = (uint32_t)(w >> (BITS * i)) & (uint32_t)((1ull << BITS) - 1u);
+    r[i] = KIND == MXB_KIND_FLOAT ? __fmul_rn(tbl[raw & 15u], s) : dequant_code<BITS, KIND>(raw, s);
+  }
   if (e0 + 4 <= n) {
     __stcs(reinterpret_cast<float4*>(out + e0), make_float4(r[0], r[1], r[2], r[3]));
   } else {
@@ -353,6 +366,11 @@ __global__ void __launch_bounds__(256) dequant_vec_kernel(const uint8_t* __restr
                                                           int64_t n, int block,
                                                           float* __restrict__ out) {
   constexpr int U = 4;
+  __shared__ float tbl[16];  // float4 grid (see dequant_vec8_kernel)
+  if (KIND == MXB_KIND_FLOAT) {
+    if (threadIdx.x < 16) tbl[threadIdx.x] = f4_grid((int)threadIdx.x);
+    __syncthreads();
+  }
   const int64_t ngroups = (n + 3) / 4;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < ngroups; t += U * stride) {
@@ -371,7 +389,7 @@ __global__ void __launch_bounds__(256) dequant_vec_kernel(const uint8_t* __restr
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t g = t + u * stride;
-      if (g < ngroups) dequant4_store<BITS, KIND>(w[u], sc[u], g * 4, n, out);
+      if (g < ngroups) dequant4_store<BITS, KIND>(w[u], sc[u], g * 4, n, out, tbl);
     }
   }
 }
@@ -679,11 +697,11 @@ int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_
   const size_t in_align = BITS == 16 ? 16 : (BITS == 8 ? 8 : (BITS == 4 ? 4 : (BITS == 2 ? 2 : 1)));
   if (block % 8 == 0 && aligned(packed, in_align) && aligned(out, 16)) {
     // Measured at 2^26 elements (fraction of HBM copy bandwidth): the
-    // 4-element kernel reaches 0.75-0.79 for int2/int4/int8 (0.57-0.67 with
-    // 8 elements per lane); int1 (0.52 vs 0.47) and float4 (0.59 vs 0.49),
-    // where the decode costs more per element, keep the 8-element one.
+    // 4-element kernel reaches 0.75-0.79 for int2/int4/int8 and 0.78 for
+    // float4 (grid values from shared memory); int1 keeps the 8-element one
+    // (0.52 vs 0.47).
 #ifndef MXB_DQ8_MASK
-#define MXB_DQ8_MASK 0x3  // bit 0: float4, bit 1: int1 take the 8-element kernel
+#define MXB_DQ8_MASK 0x2  // bit 0: float4, bit 1: int1 take the 8-element kernel
 #endif
     constexpr bool v8 = (KIND == MXB_KIND_FLOAT && (MXB_DQ8_MASK & 1)) ||
                         (KIND == MXB_KIND_INT && BITS == 1 && (MXB_DQ8_MASK & 2)) ||
