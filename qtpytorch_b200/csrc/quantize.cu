@@ -394,6 +394,49 @@ __global__ void __launch_bounds__(256) dequant_vec_kernel(const uint8_t* __restr
   }
 }
 
+// Warp-chunk dequantize (BITS <= 8): one warp per chunk of 32 packed words
+// (128 code bytes, 1024/BITS elements).  The warp reads the chunk as one
+// coalesced word per lane, then writes 8/BITS float4 rows of 128 elements;
+// each lane takes the 4*BITS code bits of its 4 elements from the word that
+// holds them by shuffle, so every store instruction covers 512 contiguous
+// bytes.  The word past the end of the packed buffer is read byte by byte.
+template <int BITS, int KIND>
+__global__ void __launch_bounds__(256) dequant_warp_kernel(const uint8_t* __restrict__ packed,
+                                                           const float* __restrict__ scales,
+                                                           int64_t n, int block,
+                                                           float* __restrict__ out) {
+  constexpr int kChunk = 1024 / BITS;
+  constexpr int kRows = 8 / BITS;
+  __shared__ float tbl[16];  // float4 grid (see dequant_vec8_kernel)
+  if (KIND == MXB_KIND_FLOAT) {
+    if (threadIdx.x < 16) tbl[threadIdx.x] = f4_grid((int)threadIdx.x);
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t nbytes = (n * BITS + 7) / 8;
+  const int64_t nchunks = (n + kChunk - 1) / kChunk;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t c = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks;
+       c += nwarps) {
+    const int64_t b0 = (c * 32 + lane) * 4;
+    uint32_t word = 0u;
+    if (b0 + 4 <= nbytes) {
+      word = __ldcs(reinterpret_cast<const uint32_t*>(packed + b0));
+    } else {
+      for (int i = 0; i < 4; ++i)
+        if (b0 + i < nbytes) word |= (uint32_t)packed[b0 + i] << (8 * i);
+    }
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+      const uint32_t src = __shfl_sync(0xffffffffu, word, j * 4 * BITS + (lane * BITS) / 8);
+      const int64_t e0 = c * kChunk + j * 128 + lane * 4;
+      if (e0 < n)
+        dequant4_store<BITS, KIND>(src >> ((lane * 4 * BITS) & 31), __ldg(scales + e0 / block),
+                                   e0, n, out, tbl);
+    }
+  }
+}
+
 template <int BITS, int KIND>
 __global__ void __launch_bounds__(256) dequant_generic_kernel(const uint8_t* __restrict__ packed,
                                                               const float* __restrict__ scales,
@@ -697,9 +740,12 @@ int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_
   const size_t in_align = BITS == 16 ? 16 : (BITS == 8 ? 8 : (BITS == 4 ? 4 : (BITS == 2 ? 2 : 1)));
   if (block % 8 == 0 && aligned(packed, in_align) && aligned(out, 16)) {
     // Measured at 2^26 elements (fraction of HBM copy bandwidth): the
-    // 4-element kernel reaches 0.75-0.79 for int2/int4/int8 and 0.78 for
-    // float4 (grid values from shared memory); int1 keeps the 8-element one
-    // (0.52 vs 0.47).
+    // 4-element kernel reaches 0.75-0.79 for int2/int4/int8 and 0.77 for
+    // float4 (grid values from shared memory).  int1 takes the warp-chunk
+    // kernel: 0.84, against 0.53 for the 8-element and 0.52 for the
+    // 4-element kernel.  The warp-chunk kernel is slower for the wider codes
+    // (int2 0.73, int4 0.59, int8 0.61, float4 0.58): a lane's word then
+    // feeds only 8/BITS stores.
 #ifndef MXB_DQ8_MASK
 #define MXB_DQ8_MASK 0x2  // bit 0: float4, bit 1: int1 take the 8-element kernel
 #endif
@@ -709,7 +755,15 @@ int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_
                         (KIND == MXB_KIND_INT && BITS == 4 && (MXB_DQ8_MASK & 8)) ||
                         (KIND == MXB_KIND_INT && BITS == 8 && (MXB_DQ8_MASK & 16)) ||
                         (KIND == MXB_KIND_INT && BITS == 16 && (MXB_DQ8_MASK & 32));
-    if (v8)
+#ifndef MXB_DQW_MASK
+#define MXB_DQW_MASK 0x1  // bit per width (1, 2, 4, 8 bits) taking the warp-chunk kernel
+#endif
+    constexpr bool warp = BITS <= 8 && ((MXB_DQW_MASK >> (BITS == 1 ? 0 : BITS == 2 ? 1 :
+                                                           BITS == 4 ? 2 : 3)) & 1);
+    if (warp && aligned(packed, 4))
+      dequant_warp_kernel<BITS, KIND><<<grid_for(cdiv(n * BITS, 32)), 256, 0, st>>>(
+          packed, scales, n, block, out);
+    else if (v8)
       dequant_vec8_kernel<BITS, KIND><<<grid_for(cdiv(n, 16)), 256, 0, st>>>(packed, scales, n,
                                                                             block, out);
     else
