@@ -394,19 +394,20 @@ __global__ void __launch_bounds__(256) dequant_vec_kernel(const uint8_t* __restr
   }
 }
 
-// Warp-chunk dequantize (BITS <= 8): one warp per chunk of 32 packed words
-// (128 code bytes, 1024/BITS elements).  The warp reads the chunk as one
-// coalesced word per lane, then writes 8/BITS float4 rows of 128 elements;
-// each lane takes the 4*BITS code bits of its 4 elements from the word that
-// holds them by shuffle, so every store instruction covers 512 contiguous
-// bytes.  The word past the end of the packed buffer is read byte by byte.
+// Warp-chunk dequantize (BITS <= 8): one warp per 1024-element chunk,
+// 32*BITS packed words.  Lane l reads words l, l+32, ... (BITS coalesced
+// 128-byte warp loads), then the warp writes 8 float4 rows of 128 elements.
+// Row j's 4 codes for lane l start at chunk bit 4*BITS*(32j + l), i.e. in
+// word j*4*BITS + l*BITS/8: register (j*4*BITS)/32 of lane (that word) % 32,
+// a register index fixed per row, so one shuffle delivers it.  Every store
+// instruction covers 512 contiguous bytes.  Words past the end of the packed
+// buffer are read byte by byte.
 template <int BITS, int KIND>
 __global__ void __launch_bounds__(256) dequant_warp_kernel(const uint8_t* __restrict__ packed,
                                                            const float* __restrict__ scales,
                                                            int64_t n, int block,
                                                            float* __restrict__ out) {
-  constexpr int kChunk = 1024 / BITS;
-  constexpr int kRows = 8 / BITS;
+  static_assert(BITS <= 8, "warp-chunk dequantize covers codes up to 8 bits");
   __shared__ float tbl[16];  // float4 grid (see dequant_vec8_kernel)
   if (KIND == MXB_KIND_FLOAT) {
     if (threadIdx.x < 16) tbl[threadIdx.x] = f4_grid((int)threadIdx.x);
@@ -414,22 +415,28 @@ __global__ void __launch_bounds__(256) dequant_warp_kernel(const uint8_t* __rest
   }
   const int lane = threadIdx.x & 31;
   const int64_t nbytes = (n * BITS + 7) / 8;
-  const int64_t nchunks = (n + kChunk - 1) / kChunk;
+  const int64_t nchunks = (n + 1023) / 1024;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t c = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks;
        c += nwarps) {
-    const int64_t b0 = (c * 32 + lane) * 4;
-    uint32_t word = 0u;
-    if (b0 + 4 <= nbytes) {
-      word = __ldcs(reinterpret_cast<const uint32_t*>(packed + b0));
-    } else {
-      for (int i = 0; i < 4; ++i)
-        if (b0 + i < nbytes) word |= (uint32_t)packed[b0 + i] << (8 * i);
+    uint32_t word[BITS];
+#pragma unroll
+    for (int k = 0; k < BITS; ++k) {
+      const int64_t b0 = ((c * BITS + k) * 32 + lane) * 4;
+      word[k] = 0u;
+      if (b0 + 4 <= nbytes) {
+        word[k] = __ldcs(reinterpret_cast<const uint32_t*>(packed + b0));
+      } else {
+        for (int i = 0; i < 4; ++i)
+          if (b0 + i < nbytes) word[k] |= (uint32_t)packed[b0 + i] << (8 * i);
+      }
     }
 #pragma unroll
-    for (int j = 0; j < kRows; ++j) {
-      const uint32_t src = __shfl_sync(0xffffffffu, word, j * 4 * BITS + (lane * BITS) / 8);
-      const int64_t e0 = c * kChunk + j * 128 + lane * 4;
+    for (int j = 0; j < 8; ++j) {
+      constexpr int kRowWords = 4 * BITS;  // packed words per 128-element row
+      const uint32_t src = __shfl_sync(0xffffffffu, word[(j * kRowWords) >> 5],
+                                       ((j * kRowWords) & 31) + (lane * BITS) / 8);
+      const int64_t e0 = c * 1024 + j * 128 + lane * 4;
       if (e0 < n)
         dequant4_store<BITS, KIND>(src >> ((lane * 4 * BITS) & 31), __ldg(scales + e0 / block),
                                    e0, n, out, tbl);
@@ -740,12 +747,10 @@ int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_
   const size_t in_align = BITS == 16 ? 16 : (BITS == 8 ? 8 : (BITS == 4 ? 4 : (BITS == 2 ? 2 : 1)));
   if (block % 8 == 0 && aligned(packed, in_align) && aligned(out, 16)) {
     // Measured at 2^26 elements (fraction of HBM copy bandwidth): the
-    // 4-element kernel reaches 0.75-0.79 for int2/int4/int8 and 0.77 for
-    // float4 (grid values from shared memory).  int1 takes the warp-chunk
-    // kernel: 0.84, against 0.53 for the 8-element and 0.52 for the
-    // 4-element kernel.  The warp-chunk kernel is slower for the wider codes
-    // (int2 0.73, int4 0.59, int8 0.61, float4 0.58): a lane's word then
-    // feeds only 8/BITS stores.
+    // warp-chunk kernel reaches int1/int2/int4/int8/float4 0.84/0.84/0.82/
+    // 0.85/0.82, against 0.53 (8 elements per lane) and 0.75-0.79 (4 per
+    // lane) for the per-lane kernels, which remain for 16-bit codes and for
+    // packed buffers not 4-byte aligned.
 #ifndef MXB_DQ8_MASK
 #define MXB_DQ8_MASK 0x2  // bit 0: float4, bit 1: int1 take the 8-element kernel
 #endif
@@ -756,12 +761,12 @@ int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_
                         (KIND == MXB_KIND_INT && BITS == 8 && (MXB_DQ8_MASK & 16)) ||
                         (KIND == MXB_KIND_INT && BITS == 16 && (MXB_DQ8_MASK & 32));
 #ifndef MXB_DQW_MASK
-#define MXB_DQW_MASK 0x1  // bit per width (1, 2, 4, 8 bits) taking the warp-chunk kernel
+#define MXB_DQW_MASK 0xf  // bit per width (1, 2, 4, 8 bits) taking the warp-chunk kernel
 #endif
     constexpr bool warp = BITS <= 8 && ((MXB_DQW_MASK >> (BITS == 1 ? 0 : BITS == 2 ? 1 :
                                                            BITS == 4 ? 2 : 3)) & 1);
     if (warp && aligned(packed, 4))
-      dequant_warp_kernel<BITS, KIND><<<grid_for(cdiv(n * BITS, 32)), 256, 0, st>>>(
+      dequant_warp_kernel<(BITS <= 8 ? BITS : 8), KIND><<<grid_for(cdiv(n, 32)), 256, 0, st>>>(
           packed, scales, n, block, out);
     else if (v8)
       dequant_vec8_kernel<BITS, KIND><<<grid_for(cdiv(n, 16)), 256, 0, st>>>(packed, scales, n,
