@@ -246,7 +246,7 @@ def run_ours(args, world, rank, local):
     def flush():
         flush_buf.zero_()
 
-    if args.only in ("gemv1", "gemv16", "wo2048", "quant"):
+    if args.only in ("gemv1", "gemv16", "wo2048", "quant", "dequant"):
         print(json.dumps(run_extras(args, dev, flush, torch.cuda.current_stream(dev), hbm, bf16)))
         return
 
@@ -419,6 +419,13 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
             ops.quantize(x, mxb.int4d, 128)
         torch.cuda.synchronize()
         return {"only": "quant"}
+    if args.only == "dequant":  # profiling case: int4d dequantize of 2^26 values
+        x = torch.randn(1 << 26, device=dev)
+        p_, s_, _ = ops.quantize(x, mxb.int4d, 128)
+        for _ in range(3 + args.steps):
+            ops.dequantize(p_, s_, mxb.int4d, 1 << 26, 128)
+        torch.cuda.synchronize()
+        return {"only": "dequant"}
     g = torch.Generator().manual_seed(1)
     W = torch.randn(11008, 4096, generator=g) * 0.02
     lin = torch.nn.Linear(4096, 11008, bias=False)
@@ -520,7 +527,7 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="N > 1: output gather fused into the GEMM kernel, or NCCL all-gather")
-    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant"],
+    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant", "dequant"],
                     help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
