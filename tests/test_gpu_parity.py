@@ -62,6 +62,48 @@ def test_dequantize_ragged(n, dt, block):
     assert np.array_equal(_u32(dq), _u32(ref))
 
 
+@pytest.mark.parametrize("in_dt", [torch.float32, torch.bfloat16])
+def test_quantize_float4_near_boundaries(in_dt):
+    """float4 codes for values within 4 ulp of every rounding boundary (and
+    of a 2^-20 quotient) times the block absmax, over divisors with extreme
+    mantissas (all ones, all zeros) and exponents 2^-39..2^127, plus signed
+    zeros and a subnormal: the bucket of the IEEE quotient everywhere."""
+    rng = np.random.default_rng(11)
+    nblk, block = 8192, 128
+    mant = rng.integers(0, 1 << 23, nblk, dtype=np.uint32)
+    mant[:512] = 0x7FFFFF
+    mant[512:1024] = 0
+    mant[1024:1536] = 0x7FFFFF ^ rng.integers(0, 8, 512, dtype=np.uint32)
+    ex = rng.integers(127 - 39, 127 + 127, nblk, dtype=np.uint32)
+    ex[:64] = 127 + 125
+    ex[64:128] = 127 + 126
+    a = ((ex << 23) | mant).view(np.float32)
+    if in_dt == torch.bfloat16:
+        a = (a.view(np.uint32) & 0xFFFF0000).view(np.float32)
+    mids = O.minifloat4_mids()
+    targets = np.concatenate([mids[mids > 0], np.float32([2.0 ** -20])]).astype(np.float32)
+    prod = (a[:, None].astype(np.float64) * targets[None, :]).astype(np.float32)
+    offs = np.arange(-4, 5, dtype=np.int64)
+    bits = prod.view(np.int32)[:, :, None].astype(np.int64) + offs[None, None, :]
+    vals = bits.astype(np.int32).view(np.float32).reshape(nblk, -1)
+    vals = np.abs(vals) * np.where(rng.random(vals.shape) < 0.5, -1, 1).astype(np.float32)
+    blk = np.zeros((nblk, block), np.float32)
+    take = min(vals.shape[1], block - 4)
+    blk[:, 0] = a * np.where(rng.random(nblk) < 0.5, -1, 1).astype(np.float32)
+    blk[:, 1:1 + take] = vals[:, :take]
+    blk[:, block - 3] = 0.0
+    blk[:, block - 2] = -0.0
+    blk[:, block - 1] = np.float32(1e-45)
+    x = torch.from_numpy(blk.reshape(-1)).to(in_dt)
+    xf = x.float().numpy()
+    assert np.all(np.abs(xf.reshape(nblk, block)).max(axis=1) == np.abs(xf.reshape(nblk, block)[:, 0]))
+    d = get_mx_dtype("float4d")
+    q = mxb.mx_tensor.quantize(x.cuda(), d, block)
+    p, s, _ = O.quantize(xf, d.bits, d.kind, block)
+    assert np.array_equal(q._mx_scales.cpu().numpy(), s)
+    assert np.array_equal(q._mx_packed.cpu().numpy(), p)
+
+
 @pytest.mark.parametrize("offset", [1, 3])
 def test_quantize_unaligned_views(offset):
     # pointers not 16-byte aligned take the scalar-load path
