@@ -166,14 +166,56 @@ __global__ void __launch_bounds__(256) quant_vec_kernel(const InT* __restrict__ 
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t w = warp0; w * 32 < groups; w += nwarps) {
-    const int64_t t = w * 32 + lane;
-    const bool valid = t < groups;
-    float v[E];
+#ifndef MXB_Q_BF16_PREFETCH
+#define MXB_Q_BF16_PREFETCH 1
+#endif
+  if constexpr (sizeof(InT) == 2 && MXB_Q_BF16_PREFETCH) {
+    // bf16: a lane's E inputs are only 2E bytes, so the next iteration's
+    // words are loaded before this one is quantized (twice the bytes in
+    // flight per lane).  Lanes whose group is not whole take load8.
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    uint4 raw[E / 8];
+    auto fetch = [&](int64_t tt) {
+      if (vec && tt * E + E <= n) {
 #pragma unroll
-    for (int h = 0; h < E / 8; ++h)
-      load8<InT>(x, t * E + 8 * h, valid ? n : 0, vec, *reinterpret_cast<float(*)[8]>(v + 8 * h));
-    quant8_store<BITS, MODE, E>(v, valid, L, t * E, packed, scales, t / L);
+        for (int h = 0; h < E / 8; ++h) raw[h] = __ldcs(xv + (tt * E) / 8 + h);
+      }
+    };
+    fetch(warp0 * 32 + lane);
+    for (int64_t w = warp0; w * 32 < groups; w += nwarps) {
+      const int64_t t = w * 32 + lane;
+      const bool valid = t < groups;
+      float v[E];
+      if (vec && t * E + E <= n) {
+#pragma unroll
+        for (int h = 0; h < E / 8; ++h) {
+          const uint32_t wd[4] = {raw[h].x, raw[h].y, raw[h].z, raw[h].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            v[8 * h + 2 * i] = __uint_as_float(wd[i] << 16);
+            v[8 * h + 2 * i + 1] = __uint_as_float(wd[i] & 0xffff0000u);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < E / 8; ++h)
+          load8<InT>(x, t * E + 8 * h, valid ? n : 0, vec,
+                     *reinterpret_cast<float(*)[8]>(v + 8 * h));
+      }
+      fetch(t + nwarps * 32);
+      quant8_store<BITS, MODE, E>(v, valid, L, t * E, packed, scales, t / L);
+    }
+  } else {
+    for (int64_t w = warp0; w * 32 < groups; w += nwarps) {
+      const int64_t t = w * 32 + lane;
+      const bool valid = t < groups;
+      float v[E];
+#pragma unroll
+      for (int h = 0; h < E / 8; ++h)
+        load8<InT>(x, t * E + 8 * h, valid ? n : 0, vec,
+                   *reinterpret_cast<float(*)[8]>(v + 8 * h));
+      quant8_store<BITS, MODE, E>(v, valid, L, t * E, packed, scales, t / L);
+    }
   }
 }
 

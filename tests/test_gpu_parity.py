@@ -49,13 +49,17 @@ def test_quantize_bit_exact(golden, c):
 @pytest.mark.parametrize("n", [8, 1000, 1024, 1032, 4104, 33000, (1 << 20) + 24])
 @pytest.mark.parametrize("dt", ["int1d", "int2d", "int4d", "int8d", "float4d"])
 @pytest.mark.parametrize("block", [8, 32, 128])
-def test_dequantize_ragged(n, dt, block):
-    """Vectorised dequantize kernels at lengths that end inside a 1024-element
-    chunk, a packed word and a scale block."""
+@pytest.mark.parametrize("in_dt", [torch.float32, torch.bfloat16])
+def test_dequantize_ragged(n, dt, block, in_dt):
+    """Vectorised quantize and dequantize kernels at lengths that end inside
+    a 1024-element chunk, a packed word and a scale block."""
     d = get_mx_dtype(dt)
     g = torch.Generator().manual_seed(n + block)
-    x = torch.randn(n, generator=g)
+    x = torch.randn(n, generator=g).to(in_dt)
     q = mxb.mx_tensor.quantize(x.cuda(), d, block)
+    p, s, _ = O.quantize(x.float().numpy(), d.bits, d.kind, block)
+    assert np.array_equal(q._mx_packed.cpu().numpy(), p)
+    assert np.array_equal(_u32(q._mx_scales.cpu().numpy()), _u32(s))
     dq = q.dequantize().cpu().numpy()
     ref = O.dequantize(q._mx_packed.cpu().numpy(), q._mx_scales.cpu().numpy(), d.bits, d.kind,
                        (n,), block)
