@@ -94,6 +94,26 @@ int mxb_quantize(const void* x, int x_dtype, int64_t n, int64_t row_len, int bit
                  int kind, int variant, int block, const float* signs, void* packed,
                  float* scales, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Workspace bytes mxb_dynamic_quantize needs (0 when block is 8..256). */
+size_t mxb_dynamic_quantize_workspace_size(int64_t n, int64_t block);
+
+/*
+ * Dynamic (runtime) integer quantize over flat blocks of any length.
+ * Replaces mxtorch `dynamic_quantize` (mxtorch.py:2665-2712): "per_token"
+ * is block = the last dim (one scale per row), "per_tensor" block = n,
+ * "per_block" block = the given block.  scale = max(amax, 1e-12) / max_int
+ * (a true division), codes = round-half-even(x / scale), packed like
+ * `bit_packer.pack_auto`.
+ *   x        device, n elements of x_dtype (MXB_F32 / MXB_BF16)
+ *   bits     2, 4, 8 or 16 (int1 has max_int 0 in the reference: rejected)
+ *   packed   mxb_packed_bytes(n, bits, block) bytes
+ *   scales   ceil(n / block) floats
+ * Bit-identical to the reference's CPU arithmetic.
+ */
+int mxb_dynamic_quantize(const void* x, int x_dtype, int64_t n, int64_t block, int bits,
+                         void* packed, float* scales, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
 /*
  * Unpack + dequantize to fp32.
  * Replaces mxtorch `_dequant` (mxtorch.py:1530-1597).  bits may also be 16

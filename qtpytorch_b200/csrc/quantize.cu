@@ -12,6 +12,7 @@
 #include "mxb_common.cuh"
 
 #include <math.h>
+#include <stdint.h>
 #include <string.h>
 
 #include <atomic>
@@ -876,6 +877,45 @@ size_t mxb_quantize_workspace_size(int64_t n, int64_t row_len, int bits, int kin
   if (variant != MXB_VAR_H) return flat;
   if (vec_block(block) && row_len > 0 && row_len % block == 0) return 0;
   return (((size_t)n * sizeof(float) + 255) & ~(size_t)255) + flat;
+}
+
+size_t mxb_dynamic_quantize_workspace_size(int64_t n, int64_t block) {
+  if (n <= 0 || block <= 0 || block > INT32_MAX) return 0;
+  return vec_block((int)block) ? 0 : (size_t)cdiv(n, block) * sizeof(float);
+}
+
+// Per-token / per-tensor quantize: scale = max(amax, 1e-12) / max_int by
+// true division, codes = round-half-even(x / scale) (the matmul
+// requantization's arithmetic), over flat blocks of any length.
+int mxb_dynamic_quantize(const void* x, int x_dtype, int64_t n, int64_t block, int bits,
+                         void* packed, float* scales, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (bits != 2 && bits != 4 && bits != 8 && bits != 16) return MXB_E_DTYPE;
+  if (n < 0 || block <= 0 || block > INT32_MAX) return MXB_E_SHAPE;
+  if (n == 0) return MXB_OK;
+  if (!x || !packed || !scales) return MXB_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* p = static_cast<uint8_t*>(packed);
+  const int b = (int)block;
+  if (x_dtype == MXB_F32) {
+    const float* xf = static_cast<const float*>(x);
+    switch (bits) {
+      case 2: return quant_flat<float, 2, Q_INT_DIV>(xf, n, b, p, scales, workspace, workspace_bytes, st);
+      case 4: return quant_flat<float, 4, Q_INT_DIV>(xf, n, b, p, scales, workspace, workspace_bytes, st);
+      case 8: return quant_flat<float, 8, Q_INT_DIV>(xf, n, b, p, scales, workspace, workspace_bytes, st);
+      default: return quant_flat<float, 16, Q_INT_DIV>(xf, n, b, p, scales, workspace, workspace_bytes, st);
+    }
+  }
+  if (x_dtype == MXB_BF16) {
+    const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+    switch (bits) {
+      case 2: return quant_flat<__nv_bfloat16, 2, Q_INT_DIV>(xb, n, b, p, scales, workspace, workspace_bytes, st);
+      case 4: return quant_flat<__nv_bfloat16, 4, Q_INT_DIV>(xb, n, b, p, scales, workspace, workspace_bytes, st);
+      case 8: return quant_flat<__nv_bfloat16, 8, Q_INT_DIV>(xb, n, b, p, scales, workspace, workspace_bytes, st);
+      default: return quant_flat<__nv_bfloat16, 16, Q_INT_DIV>(xb, n, b, p, scales, workspace, workspace_bytes, st);
+    }
+  }
+  return MXB_E_DTYPE;
 }
 
 int mxb_quantize(const void* x, int x_dtype, int64_t n, int64_t row_len, int bits, int kind,

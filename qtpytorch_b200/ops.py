@@ -133,7 +133,8 @@ def qgemm(a_packed, a_scales, b_packed, b_scales, M: int, K: int, N: int, bits: 
     """Packed integer matmul (mxtorch.py:5497-5573 CPU branch, bit-exact).
 
     Returns (c_packed, c_scales, c_f32 or None); c_packed is int32 words for
-    16-bit codes, int8 bytes otherwise.  ``b_kmajor``: b_packed / b_scales
+    16-bit codes, int8 bytes otherwise.  out_bits 32: (None, None, c_f32),
+    the fp32 C without requantization.  ``b_kmajor``: b_packed / b_scales
     hold B^T [N, K] quantized along K (each element with its own block's
     scale), computed by ``mxb_qgemm_kmajor``.
     """
@@ -141,12 +142,17 @@ def qgemm(a_packed, a_scales, b_packed, b_scales, M: int, K: int, N: int, bits: 
     dev = a_packed.device
     lib = L.load()
     nb = -(-(M * N) // block)
-    nbytes = lib.mxb_packed_bytes(M * N, out_bits, block)
-    if out_bits == 16:
-        c_packed = torch.empty(nbytes // 4, dtype=torch.int32, device=dev)
+    if out_bits == 32:  # the fp32 C alone, no requantization
+        c_packed = c_scales = None
+        want_f32 = True
+    elif out_bits == 16:
+        c_packed = torch.empty(lib.mxb_packed_bytes(M * N, 16, block) // 4, dtype=torch.int32,
+                               device=dev)
     else:
-        c_packed = torch.empty(nbytes, dtype=torch.int8, device=dev)
-    c_scales = torch.empty(nb, dtype=torch.float32, device=dev)
+        c_packed = torch.empty(lib.mxb_packed_bytes(M * N, out_bits, block), dtype=torch.int8,
+                               device=dev)
+    if out_bits != 32:
+        c_scales = torch.empty(nb, dtype=torch.float32, device=dev)
     c_f32 = torch.empty(M, N, dtype=torch.float32, device=dev) if want_f32 else None
     wsf = lib.mxb_qgemm_kmajor_workspace_size if b_kmajor else lib.mxb_qgemm_workspace_size
     fn = lib.mxb_qgemm_kmajor if b_kmajor else lib.mxb_qgemm
@@ -187,3 +193,32 @@ def linear_wonly(x: torch.Tensor, w_packed: torch.Tensor, w_scales: torch.Tensor
                                   L.stream_of(dev))
     L.check(rc, f"mxb_linear_wonly({M}x{K}x{N}, {dt.name})")
     return y
+
+
+def dynamic_quantize(x: torch.Tensor, bits: int, block: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(packed, scales) of ``mxb_dynamic_quantize``: flat blocks of any
+    length, scale = max(amax, 1e-12) / max_int, codes = rint(x / scale)
+    (mxtorch.py:2665-2712).  packed is int32 words for 16-bit codes."""
+    dev = _device_of(x)
+    x = x.detach()
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float()
+    x = x.to(dev).contiguous()
+    n = x.numel()
+    lib = L.load()
+    nbytes = lib.mxb_packed_bytes(n, bits, block)
+    if bits == 16:
+        packed = torch.empty(nbytes // 4, dtype=torch.int32, device=dev)
+    else:
+        packed = torch.empty(nbytes, dtype=torch.int8, device=dev)
+    scales = torch.empty(-(-n // block), dtype=torch.float32, device=dev)
+    if n == 0:
+        return packed, scales
+    wsb = lib.mxb_dynamic_quantize_workspace_size(n, block)
+    ws = L.workspace(wsb, dev)
+    in_t = L.BF16 if x.dtype == torch.bfloat16 else L.F32
+    with torch.cuda.device(dev):
+        rc = lib.mxb_dynamic_quantize(L.ptr(x), in_t, n, block, bits, L.ptr(packed),
+                                      L.ptr(scales), L.ptr(ws), wsb, L.stream_of(dev))
+    L.check(rc, f"mxb_dynamic_quantize(n={n}, block={block}, bits={bits})")
+    return packed, scales

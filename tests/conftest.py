@@ -17,3 +17,9 @@ def pytest_configure(config):
 def golden():
     import numpy as np
     return np.load(os.path.join(ROOT, "tests", "golden", "golden.npz"))
+
+
+@pytest.fixture(scope="session")
+def golden_dynamic():
+    import numpy as np
+    return np.load(os.path.join(ROOT, "tests", "golden", "golden_dynamic.npz"))

@@ -1,0 +1,114 @@
+"""Golden vectors for the dynamic-quantize / full-int8 linear path, made by
+running the reference mxtorch CPU path (not needed at test time).
+
+    PYTHONHASHSEED=0 PYTHONDONTWRITEBYTECODE=1 \
+        python tests/golden/make_golden_dynamic.py /path/to/qtpytorch
+
+Covers ``dynamic_quantize`` (mxtorch.py:2665-2712, every granularity),
+``fused_int8_linear`` (3910-3960, CPU branch: dequantize + F.linear) and
+``mx_dynamic_linear`` (8870-8978).  Inputs come from torch's CPU generator
+with the seeds in ``DYN_CASES`` / ``FUSED_CASES`` / ``DLIN_CASES`` so the
+tests regenerate them.  Output: ``tests/golden/golden_dynamic.npz``.
+"""
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+# key, dtype, granularity, shape, seed, input dtype, block (per_block only)
+DYN_CASES = [
+    ("tok_int8d", "int8d", "per_token", (16, 256), 101, "fp32", 64),
+    ("tok_int4d", "int4d", "per_token", (8, 384), 102, "fp32", 64),
+    ("tok_int2d", "int2d", "per_token", (8, 130), 103, "fp32", 64),
+    ("tok_int8d_bf16", "int8d", "per_token", (4, 512), 104, "bf16", 64),
+    ("tok_int8d_3d", "int8d", "per_token", (2, 3, 96), 105, "fp32", 64),
+    ("tensor_int8d", "int8d", "per_tensor", (1000,), 106, "fp32", 64),
+    ("tensor_int4d", "int4d", "per_tensor", (7, 33), 107, "fp32", 64),
+    ("block_int8d", "int8d", "per_block", (4, 256), 108, "fp32", 64),
+    ("chan_int8d", "int8d", "per_channel", (64, 32), 109, "fp32", 64),
+]
+
+# key, M, K, N, x granularity, weight block, bias, seed
+FUSED_CASES = [
+    ("f_tok_b128", 8, 256, 96, "per_token", 128, True, 201),
+    ("f_tok_nobias", 5, 384, 64, "per_token", 128, False, 202),
+    ("f_block128", 16, 256, 128, "per_block128", 128, True, 203),
+    ("f_tc", 256, 512, 256, "per_token", 128, True, 204),
+]
+
+# key, tokens, in, out, weight dtype, bias, seed
+DLIN_CASES = [
+    ("dl_int4d", 6, 256, 96, "int4d", True, 301),
+    ("dl_int8d_nobias", 3, 128, 64, "int8d", False, 302),
+]
+
+
+def make_dyn_input(c):
+    _, _, _, shape, seed, in_dt, _ = c
+    x = torch.randn(*shape, generator=torch.Generator().manual_seed(seed)) * 2.0
+    return x.bfloat16() if in_dt == "bf16" else x
+
+
+def make_fused_inputs(c):
+    _, M, K, N, _, _, has_bias, seed = c
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g)
+    w = torch.randn(N, K, generator=g) * 0.05
+    b = torch.randn(N, generator=g) if has_bias else None
+    return x, w, b
+
+
+def make_dlin_inputs(c):
+    _, T, K, N, _, has_bias, seed = c
+    g = torch.Generator().manual_seed(seed)
+    lin = torch.nn.Linear(K, N, bias=has_bias)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(N, K, generator=g) * 0.05)
+        if has_bias:
+            lin.bias.copy_(torch.randn(N, generator=g))
+    x = torch.randn(T, K, generator=g)
+    return lin, x
+
+
+def main(ref_dir: str) -> None:
+    if os.environ.get("PYTHONHASHSEED") != "0":
+        raise SystemExit("run with PYTHONHASHSEED=0")
+    sys.path.insert(0, ref_dir)
+    import mxtorch as mx  # the reference
+
+    torch.set_num_threads(1)
+    out = {}
+    for c in DYN_CASES:
+        key, dt, gran, _, _, _, block = c
+        q = mx.dynamic_quantize(make_dyn_input(c), dt, gran, block)
+        out[f"{key}/packed"] = q._mx_packed.numpy()
+        out[f"{key}/scales"] = q._mx_scales.numpy()
+        out[f"{key}/block"] = np.int64(q._mx_block)
+        out[f"{key}/n"] = np.int64(q._mx_n)
+        out[f"{key}/dequant"] = q.dequantize().float().numpy()
+    for c in FUSED_CASES:
+        key, M, K, N, gran, wblock, _, _ = c
+        x, w, b = make_fused_inputs(c)
+        if gran == "per_token":
+            xq = mx.dynamic_quantize(x, "int8d", "per_token")
+        else:
+            xq = mx.mx_tensor.quantize(x, mx.get_mx_dtype("int8d"), 128)
+        wq = mx.mx_tensor.quantize(w, mx.get_mx_dtype("int8d"), wblock)
+        y = mx.fused_int8_linear(xq, wq, b, wblock)
+        out[f"{key}/out"] = y.numpy()
+    for c in DLIN_CASES:
+        key, _, _, _, wdt, _, _ = c
+        lin, x = make_dlin_inputs(c)
+        m = mx.mx_dynamic_linear.from_linear(lin, wdt, "int8d")
+        out[f"{key}/out"] = m(x).detach().numpy()
+        out[f"{key}/w_packed"] = m.weight._mx_packed.numpy()
+        out[f"{key}/w_scales"] = m.weight._mx_scales.numpy()
+    np.savez_compressed(os.path.join(HERE, "golden_dynamic.npz"), **out)
+    print(f"wrote {len(out)} arrays")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1])
