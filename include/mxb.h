@@ -126,6 +126,25 @@ int mxb_dequantize(const void* packed, const float* scales, int64_t n, int64_t r
                    int bits, int kind, int variant, int block, const float* signs,
                    float* out, void* stream);
 
+/*
+ * Dequantize + ReLU to fp32 (base variants): relu(_dequant(x)), NaN kept.
+ * Replaces the epilogue of mxtorch `fused_linear_relu` (mxtorch.py:4012-4074,
+ * `_k_dequant_relu` 3441-3456; the reference's CPU branch
+ * F.relu(y.dequantize()) is the formula).  Arguments as mxb_dequantize.
+ */
+int mxb_dequantize_relu(const void* packed, const float* scales, int64_t n, int bits, int kind,
+                        int block, float* out, void* stream);
+
+/*
+ * SiLU(dequant(gate)) * dequant(up) to fp32, SiLU(g) = g / (1 + exp(-g)).
+ * Replaces mxtorch `fused_silu_and_mul` (mxtorch.py:4077-4109,
+ * `_k_dequant_silu_and_mul` 3459-3479) for two packed operands of one dtype,
+ * block and length n (base variants).
+ */
+int mxb_dequantize_silu_mul(const void* gate_packed, const float* gate_scales,
+                            const void* up_packed, const float* up_scales, int64_t n, int bits,
+                            int kind, int block, float* out, void* stream);
+
 /* Randomized Hadamard transform of `rows` rows of length d (pow2ceil(d) <=
  * 32768), out-of-place or in place.  inverse=0: y = WHT(x * signs) / sqrt(n)
  * (hadamard_rotation.rotate, mxtorch.py:2866-2890); inverse=1:

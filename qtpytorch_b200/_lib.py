@@ -46,6 +46,8 @@ PROTOTYPES = {
     "mxb_dynamic_quantize_workspace_size": (_sz, [_i64, _i64]),
     "mxb_dynamic_quantize": (_int, [_vp, _int, _i64, _i64, _int, _vp, _vp, _vp, _sz, _vp]),
     "mxb_dequantize": (_int, [_vp, _vp, _i64, _i64, _int, _int, _int, _int, _vp, _vp, _vp]),
+    "mxb_dequantize_relu": (_int, [_vp, _vp, _i64, _int, _int, _int, _vp, _vp]),
+    "mxb_dequantize_silu_mul": (_int, [_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _vp, _vp]),
     "mxb_hadamard_rows": (_int, [_vp, _i64, _i64, _vp, _int, _vp, _vp]),
     "mxb_qgemm_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int]),
     "mxb_qgemm": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _int, _int, _int,

@@ -384,14 +384,31 @@ __device__ __forceinline__ uint64_t load_codes4(const uint8_t* __restrict__ pack
   }
 }
 
+// Fused activations after dequantize.  ReLU keeps NaN (torch's CPU relu
+// propagates it); SiLU(g) = g / (1 + exp(-g)).
+enum DqAct { ACT_NONE = 0, ACT_RELU = 1 };
+__device__ __forceinline__ float relu_keep_nan(float v) {
+  return v > 0.0f ? v : (v != v ? v : 0.0f);
+}
+__device__ __forceinline__ float silu(float g) { return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g))); }
+
 template <int BITS, int KIND>
-__device__ __forceinline__ void dequant4_store(uint64_t w, float s, int64_t e0, int64_t n,
-                                               float* __restrict__ out, const float* tbl) {
-  float r[4];
+__device__ __forceinline__ void dequant4(uint64_t w, float s, const float* tbl, float (&r)[4]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t raw = (uint32_t)(w >> (BITS * i)) & (uint32_t)((1ull << BITS) - 1u);
     r[i] = KIND == MXB_KIND_FLOAT ? __fmul_rn(tbl[raw & 15u], s) : dequant_code<BITS, KIND>(raw, s);
+  }
+}
+
+template <int BITS, int KIND, int ACT = ACT_NONE>
+__device__ __forceinline__ void dequant4_store(uint64_t w, float s, int64_t e0, int64_t n,
+                                               float* __restrict__ out, const float* tbl) {
+  float r[4];
+  dequant4<BITS, KIND>(w, s, tbl, r);
+  if (ACT == ACT_RELU) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = relu_keep_nan(r[i]);
   }
   if (e0 + 4 <= n) {
     __stcs(reinterpret_cast<float4*>(out + e0), make_float4(r[0], r[1], r[2], r[3]));
@@ -445,7 +462,7 @@ __global__ void __launch_bounds__(256) dequant_vec_kernel(const uint8_t* __restr
 // a register index fixed per row, so one shuffle delivers it.  Every store
 // instruction covers 512 contiguous bytes.  Words past the end of the packed
 // buffer are read byte by byte.
-template <int BITS, int KIND>
+template <int BITS, int KIND, int ACT = ACT_NONE>
 __global__ void __launch_bounds__(256) dequant_warp_kernel(const uint8_t* __restrict__ packed,
                                                            const float* __restrict__ scales,
                                                            int64_t n, int block,
@@ -481,20 +498,96 @@ __global__ void __launch_bounds__(256) dequant_warp_kernel(const uint8_t* __rest
                                        ((j * kRowWords) & 31) + (lane * BITS) / 8);
       const int64_t e0 = c * 1024 + j * 128 + lane * 4;
       if (e0 < n)
-        dequant4_store<BITS, KIND>(src >> ((lane * 4 * BITS) & 31), __ldg(scales + e0 / block),
+        dequant4_store<BITS, KIND, ACT>(src >> ((lane * 4 * BITS) & 31), __ldg(scales + e0 / block),
                                    e0, n, out, tbl);
     }
   }
 }
 
-template <int BITS, int KIND>
+template <int BITS, int KIND, int ACT = ACT_NONE>
 __global__ void __launch_bounds__(256) dequant_generic_kernel(const uint8_t* __restrict__ packed,
                                                               const float* __restrict__ scales,
                                                               int64_t n, int block,
                                                               float* __restrict__ out) {
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (int64_t)gridDim.x * blockDim.x)
-    out[e] = dequant_code<BITS, KIND>(raw_code<BITS>(packed, e), __ldg(scales + e / block));
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const float v = dequant_code<BITS, KIND>(raw_code<BITS>(packed, e), __ldg(scales + e / block));
+    out[e] = ACT == ACT_RELU ? relu_keep_nan(v) : v;
+  }
+}
+
+// SiLU(dequant(gate)) * dequant(up) (mxtorch.py:3459-3479, 4077-4109), both
+// operands of one dtype, block and length.  Same warp-chunk layout as
+// dequant_warp_kernel, over two packed streams.
+template <int BITS, int KIND>
+__global__ void __launch_bounds__(256) silu_mul_warp_kernel(
+    const uint8_t* __restrict__ gp, const float* __restrict__ gs, const uint8_t* __restrict__ up,
+    const float* __restrict__ us, int64_t n, int block, float* __restrict__ out) {
+  static_assert(BITS <= 8, "warp-chunk kernels cover codes up to 8 bits");
+  __shared__ float tbl[16];
+  if (KIND == MXB_KIND_FLOAT) {
+    if (threadIdx.x < 16) tbl[threadIdx.x] = f4_grid((int)threadIdx.x);
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t nbytes = (n * BITS + 7) / 8;
+  const int64_t nchunks = (n + 1023) / 1024;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t c = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks;
+       c += nwarps) {
+    uint32_t wg[BITS], wu[BITS];
+#pragma unroll
+    for (int k = 0; k < BITS; ++k) {
+      const int64_t b0 = ((c * BITS + k) * 32 + lane) * 4;
+      wg[k] = wu[k] = 0u;
+      if (b0 + 4 <= nbytes) {
+        wg[k] = __ldcs(reinterpret_cast<const uint32_t*>(gp + b0));
+        wu[k] = __ldcs(reinterpret_cast<const uint32_t*>(up + b0));
+      } else {
+        for (int i = 0; i < 4; ++i)
+          if (b0 + i < nbytes) {
+            wg[k] |= (uint32_t)gp[b0 + i] << (8 * i);
+            wu[k] |= (uint32_t)up[b0 + i] << (8 * i);
+          }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      constexpr int kRowWords = 4 * BITS;
+      const int reg = (j * kRowWords) >> 5;
+      const int srcl = ((j * kRowWords) & 31) + (lane * BITS) / 8;
+      const int sh = (lane * 4 * BITS) & 31;
+      const uint32_t g = __shfl_sync(0xffffffffu, wg[reg], srcl) >> sh;
+      const uint32_t u = __shfl_sync(0xffffffffu, wu[reg], srcl) >> sh;
+      const int64_t e0 = c * 1024 + j * 128 + lane * 4;
+      if (e0 < n) {
+        float rg[4], ru[4];
+        dequant4<BITS, KIND>(g, __ldg(gs + e0 / block), tbl, rg);
+        dequant4<BITS, KIND>(u, __ldg(us + e0 / block), tbl, ru);
+        float r[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r[i] = __fmul_rn(silu(rg[i]), ru[i]);
+        if (e0 + 4 <= n) {
+          __stcs(reinterpret_cast<float4*>(out + e0), make_float4(r[0], r[1], r[2], r[3]));
+        } else {
+          for (int i = 0; i < 4; ++i)
+            if (e0 + i < n) out[e0 + i] = r[i];
+        }
+      }
+    }
+  }
+}
+
+template <int BITS, int KIND>
+__global__ void __launch_bounds__(256) silu_mul_generic_kernel(
+    const uint8_t* __restrict__ gp, const float* __restrict__ gs, const uint8_t* __restrict__ up,
+    const float* __restrict__ us, int64_t n, int block, float* __restrict__ out) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const float g = dequant_code<BITS, KIND>(raw_code<BITS>(gp, e), __ldg(gs + e / block));
+    const float u = dequant_code<BITS, KIND>(raw_code<BITS>(up, e), __ldg(us + e / block));
+    out[e] = __fmul_rn(silu(g), u);
+  }
 }
 
 // ── Walsh–Hadamard transform of one row held in shared memory ────────────────
@@ -825,6 +918,32 @@ int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_
   return MXB_OK;
 }
 
+// dequantize + ReLU, and SiLU(gate) * up: the warp-chunk kernels where the
+// block is a multiple of 8 and the pointers are aligned, else per element.
+template <int BITS, int KIND>
+int dequant_relu_launch(const uint8_t* p, const float* s, int64_t n, int block, float* out,
+                        cudaStream_t st) {
+  if (BITS <= 8 && block % 8 == 0 && aligned(p, 4) && aligned(out, 16))
+    dequant_warp_kernel<(BITS <= 8 ? BITS : 8), KIND, ACT_RELU>
+        <<<grid_for(cdiv(n, 32)), 256, 0, st>>>(p, s, n, block, out);
+  else
+    dequant_generic_kernel<BITS, KIND, ACT_RELU><<<grid_for(n), 256, 0, st>>>(p, s, n, block, out);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+template <int BITS, int KIND>
+int silu_mul_launch(const uint8_t* gp, const float* gs, const uint8_t* up, const float* us,
+                    int64_t n, int block, float* out, cudaStream_t st) {
+  if (BITS <= 8 && block % 8 == 0 && aligned(gp, 4) && aligned(up, 4) && aligned(out, 16))
+    silu_mul_warp_kernel<(BITS <= 8 ? BITS : 8), KIND>
+        <<<grid_for(cdiv(n, 32)), 256, 0, st>>>(gp, gs, up, us, n, block, out);
+  else
+    silu_mul_generic_kernel<BITS, KIND><<<grid_for(n), 256, 0, st>>>(gp, gs, up, us, n, block, out);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
 }  // namespace
 
 // Used by the matmul's requantization.
@@ -956,6 +1075,47 @@ int mxb_dequantize(const void* packed, const float* scales, int64_t n, int64_t r
     case 4: return dequant_launch<4, MXB_KIND_INT>(p, scales, n, row_len, variant, block, signs, out, st);
     case 8: return dequant_launch<8, MXB_KIND_INT>(p, scales, n, row_len, variant, block, signs, out, st);
     case 16: return dequant_launch<16, MXB_KIND_INT>(p, scales, n, row_len, variant, block, signs, out, st);
+  }
+  return MXB_E_DTYPE;
+}
+
+int mxb_dequantize_relu(const void* packed, const float* scales, int64_t n, int bits, int kind,
+                        int block, float* out, void* stream) {
+  if (!(valid_dtype(bits, kind) || (bits == 16 && kind == MXB_KIND_INT))) return MXB_E_DTYPE;
+  if (n < 0 || block <= 0) return MXB_E_SHAPE;
+  if (n == 0) return MXB_OK;
+  if (!packed || !scales || !out) return MXB_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* p = static_cast<const uint8_t*>(packed);
+  if (kind == MXB_KIND_FLOAT) return dequant_relu_launch<4, MXB_KIND_FLOAT>(p, scales, n, block, out, st);
+  switch (bits) {
+    case 1: return dequant_relu_launch<1, MXB_KIND_INT>(p, scales, n, block, out, st);
+    case 2: return dequant_relu_launch<2, MXB_KIND_INT>(p, scales, n, block, out, st);
+    case 4: return dequant_relu_launch<4, MXB_KIND_INT>(p, scales, n, block, out, st);
+    case 8: return dequant_relu_launch<8, MXB_KIND_INT>(p, scales, n, block, out, st);
+    case 16: return dequant_relu_launch<16, MXB_KIND_INT>(p, scales, n, block, out, st);
+  }
+  return MXB_E_DTYPE;
+}
+
+int mxb_dequantize_silu_mul(const void* gate_packed, const float* gate_scales,
+                            const void* up_packed, const float* up_scales, int64_t n, int bits,
+                            int kind, int block, float* out, void* stream) {
+  if (!(valid_dtype(bits, kind) || (bits == 16 && kind == MXB_KIND_INT))) return MXB_E_DTYPE;
+  if (n < 0 || block <= 0) return MXB_E_SHAPE;
+  if (n == 0) return MXB_OK;
+  if (!gate_packed || !gate_scales || !up_packed || !up_scales || !out) return MXB_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* g = static_cast<const uint8_t*>(gate_packed);
+  const uint8_t* u = static_cast<const uint8_t*>(up_packed);
+  if (kind == MXB_KIND_FLOAT)
+    return silu_mul_launch<4, MXB_KIND_FLOAT>(g, gate_scales, u, up_scales, n, block, out, st);
+  switch (bits) {
+    case 1: return silu_mul_launch<1, MXB_KIND_INT>(g, gate_scales, u, up_scales, n, block, out, st);
+    case 2: return silu_mul_launch<2, MXB_KIND_INT>(g, gate_scales, u, up_scales, n, block, out, st);
+    case 4: return silu_mul_launch<4, MXB_KIND_INT>(g, gate_scales, u, up_scales, n, block, out, st);
+    case 8: return silu_mul_launch<8, MXB_KIND_INT>(g, gate_scales, u, up_scales, n, block, out, st);
+    case 16: return silu_mul_launch<16, MXB_KIND_INT>(g, gate_scales, u, up_scales, n, block, out, st);
   }
   return MXB_E_DTYPE;
 }

@@ -222,3 +222,42 @@ def dynamic_quantize(x: torch.Tensor, bits: int, block: int) -> Tuple[torch.Tens
                                       L.ptr(scales), L.ptr(ws), wsb, L.stream_of(dev))
     L.check(rc, f"mxb_dynamic_quantize(n={n}, block={block}, bits={bits})")
     return packed, scales
+
+
+def dequantize_relu(packed: torch.Tensor, scales: torch.Tensor, dt, n: int,
+                    block: int) -> torch.Tensor:
+    """relu(dequantize) in one pass (mxtorch.py:3441-3456, 4012-4074), fp32 [n]."""
+    dt = get_mx_dtype(dt)
+    if dt.variant != "":
+        raise NotImplementedError("dequantize_relu takes base dtypes")
+    L.require_cuda(packed, "dequantize_relu")
+    dev = packed.device
+    out = torch.empty(n, dtype=torch.float32, device=dev)
+    if n == 0:
+        return out
+    lib = L.load()
+    with torch.cuda.device(dev):
+        rc = lib.mxb_dequantize_relu(L.ptr(packed), L.ptr(scales.contiguous()), n, dt.bits,
+                                     _kind(dt), block, L.ptr(out), L.stream_of(dev))
+    L.check(rc, f"mxb_dequantize_relu({dt.name}, n={n})")
+    return out
+
+
+def dequantize_silu_mul(gp: torch.Tensor, gs: torch.Tensor, up: torch.Tensor, us: torch.Tensor,
+                        dt, n: int, block: int) -> torch.Tensor:
+    """SiLU(dequant(gate)) * dequant(up) in one pass (mxtorch.py:3459-3479), fp32 [n]."""
+    dt = get_mx_dtype(dt)
+    if dt.variant != "":
+        raise NotImplementedError("dequantize_silu_mul takes base dtypes")
+    L.require_cuda(gp, "dequantize_silu_mul")
+    dev = gp.device
+    out = torch.empty(n, dtype=torch.float32, device=dev)
+    if n == 0:
+        return out
+    lib = L.load()
+    with torch.cuda.device(dev):
+        rc = lib.mxb_dequantize_silu_mul(L.ptr(gp), L.ptr(gs.contiguous()), L.ptr(up.to(dev)),
+                                         L.ptr(us.to(dev).contiguous()), n, dt.bits, _kind(dt),
+                                         block, L.ptr(out), L.stream_of(dev))
+    L.check(rc, f"mxb_dequantize_silu_mul({dt.name}, n={n})")
+    return out

@@ -5,9 +5,10 @@ running the reference mxtorch CPU path (not needed at test time).
         python tests/golden/make_golden_dynamic.py /path/to/qtpytorch
 
 Covers ``dynamic_quantize`` (mxtorch.py:2665-2712, every granularity),
-``fused_int8_linear`` (3910-3960, CPU branch: dequantize + F.linear) and
-``mx_dynamic_linear`` (8870-8978).  Inputs come from torch's CPU generator
-with the seeds in ``DYN_CASES`` / ``FUSED_CASES`` / ``DLIN_CASES`` so the
+``fused_int8_linear`` (3910-3960, CPU branch: dequantize + F.linear),
+``mx_dynamic_linear`` (8870-8978), ``fused_linear_relu`` (4012-4074, CPU
+branch) and ``fused_silu_and_mul`` (4077-4109, CPU branch).  Inputs come from torch's CPU generator
+with the seeds in the ``*_CASES`` lists so the
 tests regenerate them.  Output: ``tests/golden/golden_dynamic.npz``.
 """
 import os
@@ -44,6 +45,38 @@ DLIN_CASES = [
     ("dl_int4d", 6, 256, 96, "int4d", True, 301),
     ("dl_int8d_nobias", 3, 128, 64, "int8d", False, 302),
 ]
+
+# key, M, K, N, dtype, bias, weight given as mx_tensor [in, out], seed
+RELU_CASES = [
+    ("r_int8d", 8, 256, 96, "int8d", True, False, 401),
+    ("r_int4d_mx", 5, 256, 128, "int4d", False, True, 402),
+    ("r_int8d_3d", 6, 128, 64, "int8d", True, False, 403),
+]
+
+# key, dtype, shape, block, seed
+SILU_CASES = [
+    ("s_int8d", "int8d", (8, 1000), 128, 501),
+    ("s_int4d", "int4d", (4, 4096), 128, 502),
+    ("s_float4d", "float4d", (3, 512), 32, 503),
+    ("s_int2d_b8", "int2d", (2, 96), 8, 504),
+]
+
+
+def make_relu_inputs(c):
+    key, M, K, N, _, has_bias, _, seed = c
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g)
+    if key.endswith("_3d"):
+        x = x.view(2, M // 2, K)
+    w = torch.randn(N, K, generator=g) * 0.05
+    b = torch.randn(N, generator=g) if has_bias else None
+    return x, w, b
+
+
+def make_silu_inputs(c):
+    _, _, shape, _, seed = c
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g) * 3, torch.randn(*shape, generator=g)
 
 
 def make_dyn_input(c):
@@ -106,6 +139,22 @@ def main(ref_dir: str) -> None:
         out[f"{key}/out"] = m(x).detach().numpy()
         out[f"{key}/w_packed"] = m.weight._mx_packed.numpy()
         out[f"{key}/w_scales"] = m.weight._mx_scales.numpy()
+    for c in RELU_CASES:
+        key, _, _, _, dt, _, w_mx, _ = c
+        x, w, b = make_relu_inputs(c)
+        mdt = mx.get_mx_dtype(dt)
+        if w_mx:
+            y = mx.fused_linear_relu(x, mx.mx_tensor.quantize(w.t(), mdt, 128), b, 128)
+        else:
+            y = mx.fused_linear_relu(x, w, b, 128, mdt)
+        out[f"{key}/out"] = y.numpy()
+    for c in SILU_CASES:
+        key, dt, _, block, _ = c
+        g, u = make_silu_inputs(c)
+        mdt = mx.get_mx_dtype(dt)
+        y = mx.fused_silu_and_mul(mx.mx_tensor.quantize(g, mdt, block),
+                                  mx.mx_tensor.quantize(u, mdt, block))
+        out[f"{key}/out"] = y.numpy()
     np.savez_compressed(os.path.join(HERE, "golden_dynamic.npz"), **out)
     print(f"wrote {len(out)} arrays")
 
