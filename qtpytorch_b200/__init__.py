@@ -4,7 +4,7 @@ The reference's hot-path API (DHDev0/qtpytorch ``mxtorch``) on CUDA kernels:
 ``mx_tensor.quantize`` / ``dequantize`` / ``@``, ``mx_linear``, ``to_mx``,
 ``mx_matmul``, ``get_mx_dtype``, ``register_kernel``, ``dynamic_quantize``,
 ``fused_int8_linear``, ``mx_dynamic_linear``, ``fused_linear_relu``,
-``fused_silu_and_mul``.
+``fused_silu_and_mul``, ``kv_cache_quantizer``.
 """
 from .dtypes import (  # noqa: F401
     _DTYPE_REGISTRY,
@@ -16,6 +16,7 @@ from .dtypes import *  # noqa: F401,F403  (int4d, float4d, int8dh, ...)
 from .dynamic import dynamic_quantize, fused_int8_linear, mx_dynamic_linear  # noqa: F401
 from .fused import fused_linear_relu, fused_silu_and_mul  # noqa: F401
 from .hadamard import sign_vector  # noqa: F401
+from .kv_cache import kv_cache_quantizer  # noqa: F401
 from .linear import mx_linear, to_mx  # noqa: F401
 from .tensor import mx_matmul, mx_matmul_kmajor, mx_tensor, register_kernel  # noqa: F401
 

@@ -53,8 +53,13 @@ def row_len_of(shape) -> int:
     return max(n, 1)
 
 
-def quantize(x: torch.Tensor, dt, block: int = 128) -> Tuple[torch.Tensor, torch.Tensor, int]:
-    """(packed int8, scales fp32 [nb], n): mxtorch ``quantize`` (mxtorch.py:1684-1763)."""
+def quantize(x: torch.Tensor, dt, block: int = 128,
+             out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+             ) -> Tuple[torch.Tensor, torch.Tensor, int]:
+    """(packed int8, scales fp32 [nb], n): mxtorch ``quantize`` (mxtorch.py:1684-1763).
+
+    ``out``: (packed, scales) contiguous device buffers to write into (at
+    least the packed bytes and the scale count of this call)."""
     dt = get_mx_dtype(dt)
     _check_dtype(dt)
     if block <= 0:
@@ -67,8 +72,16 @@ def quantize(x: torch.Tensor, dt, block: int = 128) -> Tuple[torch.Tensor, torch
     n = x.numel()
     nb = -(-n // block)
     lib = L.load()
-    packed = torch.empty(lib.mxb_packed_bytes(n, dt.bits, block), dtype=torch.int8, device=dev)
-    scales = torch.empty(nb, dtype=torch.float32, device=dev)
+    nbytes = lib.mxb_packed_bytes(n, dt.bits, block)
+    if out is None:
+        packed = torch.empty(nbytes, dtype=torch.int8, device=dev)
+        scales = torch.empty(nb, dtype=torch.float32, device=dev)
+    else:
+        packed, scales = out
+        if (packed.device != dev or scales.device != dev or not packed.is_contiguous()
+                or not scales.is_contiguous() or packed.numel() * packed.element_size() < nbytes
+                or scales.numel() < nb or scales.dtype != torch.float32):
+            raise ValueError("quantize: out buffers too small, not contiguous or on another device")
     if n == 0:
         return packed, scales, 0
     row_len = row_len_of(x.shape)

@@ -7,7 +7,8 @@ running the reference mxtorch CPU path (not needed at test time).
 Covers ``dynamic_quantize`` (mxtorch.py:2665-2712, every granularity),
 ``fused_int8_linear`` (3910-3960, CPU branch: dequantize + F.linear),
 ``mx_dynamic_linear`` (8870-8978), ``fused_linear_relu`` (4012-4074, CPU
-branch) and ``fused_silu_and_mul`` (4077-4109, CPU branch).  Inputs come from torch's CPU generator
+branch), ``fused_silu_and_mul`` (4077-4109, CPU branch) and
+``kv_cache_quantizer`` (2998-3119).  Inputs come from torch's CPU generator
 with the seeds in the ``*_CASES`` lists so the
 tests regenerate them.  Output: ``tests/golden/golden_dynamic.npz``.
 """
@@ -60,6 +61,22 @@ SILU_CASES = [
     ("s_float4d", "float4d", (3, 512), 32, 503),
     ("s_int2d_b8", "int2d", (2, 96), 8, 504),
 ]
+
+# key, B, H, D, dtype, max_seq_len, steps, asymmetric_v, layout, seed
+KV_CASES = [
+    ("kv_int8d", 2, 4, 64, "int8d", 16, 7, True, "bhtd", 601),
+    ("kv_int4d_evict", 1, 3, 128, "int4d", 5, 12, True, "bhtd", 602),
+    ("kv_int8d_sym", 2, 2, 32, "int8d", 70, 67, False, "bthd", 603),
+    ("kv_int4dh", 1, 2, 64, "int4dh", 8, 9, True, "bhtd", 604),
+]
+
+
+def make_kv_steps(c):
+    _, B, H, D, _, _, steps, _, layout, seed = c
+    g = torch.Generator().manual_seed(seed)
+    shape = (B, H, 1, D) if layout == "bhtd" else (B, 1, H, D)
+    return [(torch.randn(*shape, generator=g), torch.randn(*shape, generator=g) + 0.5)
+            for _ in range(steps)]
 
 
 def make_relu_inputs(c):
@@ -155,6 +172,16 @@ def main(ref_dir: str) -> None:
         y = mx.fused_silu_and_mul(mx.mx_tensor.quantize(g, mdt, block),
                                   mx.mx_tensor.quantize(u, mdt, block))
         out[f"{key}/out"] = y.numpy()
+    for c in KV_CASES:
+        key, _, H, D, dt, max_len, _, asym, _, _ = c
+        cache = mx.kv_cache_quantizer(H, D, dt, max_seq_len=max_len, asymmetric_v=asym)
+        for k, v in make_kv_steps(c):
+            cache.append_kv(k, v)
+        K, V = cache.get()
+        out[f"{key}/k"] = K.numpy()
+        out[f"{key}/v"] = V.numpy()
+        out[f"{key}/seq_len"] = np.int64(cache.seq_len)
+        out[f"{key}/memory_bytes"] = np.int64(cache.memory_bytes())
     np.savez_compressed(os.path.join(HERE, "golden_dynamic.npz"), **out)
     print(f"wrote {len(out)} arrays")
 
