@@ -8,7 +8,9 @@ Covers ``dynamic_quantize`` (mxtorch.py:2665-2712, every granularity),
 ``fused_int8_linear`` (3910-3960, CPU branch: dequantize + F.linear),
 ``mx_dynamic_linear`` (8870-8978), ``fused_linear_relu`` (4012-4074, CPU
 branch), ``fused_silu_and_mul`` (4077-4109, CPU branch) and
-``kv_cache_quantizer`` (2998-3119).  Inputs come from torch's CPU generator
+``kv_cache_quantizer`` (2998-3119); ``save_quantized`` (9860-9898) of a
+model loaded by ``load_quantized`` (9901-10004) from a plain state dict,
+written to ``ref_ckpt_int4d.pt`` (the reference's on-disk format).  Inputs come from torch's CPU generator
 with the seeds in the ``*_CASES`` lists so the
 tests regenerate them.  Output: ``tests/golden/golden_dynamic.npz``.
 """
@@ -77,6 +79,13 @@ def make_kv_steps(c):
     shape = (B, H, 1, D) if layout == "bhtd" else (B, 1, H, D)
     return [(torch.randn(*shape, generator=g), torch.randn(*shape, generator=g) + 0.5)
             for _ in range(steps)]
+
+
+def make_ckpt_model():
+    """The model class of the checkpoint fixture: Linear(64, 32), ReLU,
+    Linear(32, 16), weights from a fixed seed."""
+    torch.manual_seed(701)
+    return torch.nn.Sequential(torch.nn.Linear(64, 32), torch.nn.ReLU(), torch.nn.Linear(32, 16))
 
 
 def make_relu_inputs(c):
@@ -182,6 +191,12 @@ def main(ref_dir: str) -> None:
         out[f"{key}/v"] = V.numpy()
         out[f"{key}/seq_len"] = np.int64(cache.seq_len)
         out[f"{key}/memory_bytes"] = np.int64(cache.memory_bytes())
+    import tempfile
+    with tempfile.TemporaryDirectory() as td:
+        sd_path = os.path.join(td, "sd.pt")
+        torch.save(make_ckpt_model().state_dict(), sd_path)
+        m = mx.load_quantized(sd_path, make_ckpt_model, "int4d", 32)
+        mx.save_quantized(m, os.path.join(HERE, "ref_ckpt_int4d.pt"))
     np.savez_compressed(os.path.join(HERE, "golden_dynamic.npz"), **out)
     print(f"wrote {len(out)} arrays")
 
