@@ -63,3 +63,25 @@ def test_argument_errors_need_no_gpu():
     assert lib.mxb_linear_wonly(p, 0, 4, 128, p, p, 64, 4, 0, 128, 9, p, None, 0, None) == -6
     assert lib.mxb_linear_wonly(p, 0, 4, 128, p, p, 128, 4, 0, 128, 0, p, None, 0, None) == -7
     assert lib.mxb_hadamard_rows(p, 1, 1 << 16, p, 0, p, None) == -1
+
+
+def test_dynamic_and_epilogue_argument_errors_need_no_gpu():
+    lib = L.load()
+    p = ctypes.c_void_p(16)
+    # dynamic quantize: int1 (max_int 0 in the reference) and odd widths rejected
+    assert lib.mxb_dynamic_quantize(p, 0, 128, 128, 1, p, p, None, 0, None) == -2
+    assert lib.mxb_dynamic_quantize(p, 0, 128, 128, 3, p, p, None, 0, None) == -2
+    assert lib.mxb_dynamic_quantize(p, 0, 128, 0, 8, p, p, None, 0, None) == -1
+    assert lib.mxb_dynamic_quantize(p, 0, 128, 1 << 31, 8, p, p, None, 0, None) == -1
+    assert lib.mxb_dynamic_quantize(p, 9, 128, 128, 8, p, p, None, 0, None) == -2
+    assert lib.mxb_dynamic_quantize(None, 0, 128, 128, 8, p, p, None, 0, None) == -6
+    assert lib.mxb_dynamic_quantize(p, 0, 0, 128, 8, p, p, None, 0, None) == 0
+    assert lib.mxb_dynamic_quantize_workspace_size(1 << 20, 128) == 0
+    assert lib.mxb_dynamic_quantize_workspace_size(4096 * 3, 4096) == 3 * 4
+    # fused epilogues
+    assert lib.mxb_dequantize_relu(p, p, 128, 3, 0, 128, p, None) == -2
+    assert lib.mxb_dequantize_relu(p, p, -1, 8, 0, 128, p, None) == -1
+    assert lib.mxb_dequantize_relu(p, None, 128, 8, 0, 128, p, None) == -6
+    assert lib.mxb_dequantize_silu_mul(p, p, p, p, 128, 8, 1, 128, p, None) == -2
+    assert lib.mxb_dequantize_silu_mul(p, p, None, p, 128, 8, 0, 128, p, None) == -6
+    assert lib.mxb_dequantize_silu_mul(p, p, p, p, 0, 8, 0, 128, p, None) == 0
