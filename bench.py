@@ -321,6 +321,8 @@ def run_ours(args, world, rank, local):
     step_ms = max_over_ranks(sum(ts) / len(ts), world)
     value = 2.0 * M * N * K / (step_ms * 1e-3) / 1e12
 
+    check = check_result(step(), qa, qb, world)
+
     tg = time_steps(graphed(gemm_only, stream), args.steps, flush, stream)
     gemm_ms = max_over_ranks(sum(tg) / len(tg), world)
     int8_peak = 2.0 * bf16  # kind::i8 issues twice the bf16 rate on sm_100
@@ -400,11 +402,36 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": 2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
+            "check": check,
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
             "extra": extra,
         }
         print(json.dumps(line), flush=True)
+
+
+def check_result(c, qa, qb, world):
+    """Sampled rows of the (gathered) int16d C against a single-GPU matmul of
+    the same rows of A with the whole B, on every rank (CUDA-core kernel for
+    the 40-row sample, an implementation independent of the tcgen05 one);
+    'ok' only if every rank agrees bit for bit."""
+    from qtpytorch_b200 import ops
+    torch.cuda.synchronize()
+    dev = qa._mx_packed.device
+    rows = np.concatenate([[0, M - 1], np.random.default_rng(7).choice(M - 2, 38, replace=False) + 1])
+    r = torch.from_numpy(np.sort(rows)).to(dev)
+    a_rows = qa._mx_packed[: M * K].view(M, K)[r].contiguous()
+    s_rows = qa._mx_scales.view(M, K // BLOCK)[r].contiguous()
+    words, scales, _ = ops.qgemm(a_rows, s_rows, qb._mx_packed, qb._mx_scales, len(rows), K, N,
+                                 8, BLOCK, 16)
+    ok = (torch.equal(c._mx_packed.view(M, N // 2)[r], words.view(len(rows), N // 2))
+          and torch.equal(c._mx_scales.view(M, N // BLOCK)[r].view(torch.int32),
+                          scales.view(len(rows), N // BLOCK).view(torch.int32)))
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return "ok" if int(flag.item()) == 1 else "mismatch"
 
 
 def run_extras(args, dev, flush, stream, hbm, bf16):

@@ -273,11 +273,14 @@ int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const voi
  *   Same arguments and result as mxb_linear_wonly for the split-K shapes
  *   (1 <= M <= 16, N % 8 == 0, N % block == 0, block % 8 == 0; with bf16 x,
  *   integer codes, block % 128 == 0, N % 128 == 0 and K % 64 == 0 also
- *   M up to 32); other shapes return MXB_E_SHAPE.  Shapes whose partial
- *   sums cannot fit 16 MiB even with 256-row K splits (splits * M * N * 4
- *   bytes) return MXB_E_WORKSPACE.
+ *   M up to 32); other shapes return MXB_E_SHAPE.  The split plan is the
+ *   one mxb_linear_wonly uses, with its K splits made longer (up to the
+ *   longest the planned kernel takes) until the partial sums, splits * M *
+ *   N * 4 bytes, fit 16 MiB; shapes that still do not fit return
+ *   MXB_E_WORKSPACE.
  *   The first call on each device looks the array up (with that device
- *   current); make that first call before any stream capture.  All calls
+ *   current); make that first call before any stream capture.  A device
+ *   reset moves the array: the next call looks it up again.  All calls
  *   share the array: calls that may run at the same time on the GPU (other
  *   streams, other threads) race and must be serialized by the caller.
  *   Nothing in it needs clearing: each call writes every partial sum it reads.

@@ -20,20 +20,52 @@ constexpr size_t kScratchBytes = 16u << 20;
 static __device__ __align__(256) float g_gemv_scratch[kScratchBytes / sizeof(float)];
 
 constexpr int kMaxDevices = 64;
-constexpr int kMaxRowsPerSplit = 256;  // the split-K kernel's shared x slice
 
-// Device address of g_gemv_scratch, looked up once per device (with that
-// device current).  In host code the symbol itself is only a host-side
-// stand-in and must never be passed to a kernel.
+// cuCtxGetCurrent / cuCtxGetId through the runtime's driver entry point (no
+// libcuda link): the id of the device's current context, which changes when
+// the context is destroyed and made again (cudaDeviceReset), the one event
+// that moves the module's device array.
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+
+bool current_ctx_id(unsigned long long* id) {  // called under scratch_ptr's lock
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool looked = false;
+  if (!looked) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    looked = true;
+  }
+  void* ctx = nullptr;
+  if (!get_cur || !get_id || get_cur(&ctx) != 0 || ctx == nullptr) return false;
+  return get_id(ctx, id) == 0;
+}
+
+// Device address of g_gemv_scratch, looked up with the device current and
+// cached per device together with the id of the context it was looked up
+// in; a new context (after a device reset) looks it up again.  In host code
+// the symbol itself is only a host-side stand-in and must never be passed
+// to a kernel.
 float* scratch_ptr(int dev, int* rc) {
   static std::mutex mu;
   static float* ptrs[kMaxDevices] = {};
+  static unsigned long long ctx_ids[kMaxDevices] = {};
   if (dev < 0 || dev >= kMaxDevices) {
     *rc = MXB_E_ARG;
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(mu);
-  if (ptrs[dev] == nullptr) {
+  unsigned long long id = 0;
+  const bool have_id = current_ctx_id(&id);
+  if (ptrs[dev] == nullptr || !have_id || ctx_ids[dev] != id) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_scratch);
     if (e != cudaSuccess) {
@@ -42,6 +74,7 @@ float* scratch_ptr(int dev, int* rc) {
       return nullptr;
     }
     ptrs[dev] = static_cast<float*>(p);
+    ctx_ids[dev] = have_id ? id : 0;
   }
   *rc = MXB_OK;
   return ptrs[dev];
@@ -65,8 +98,9 @@ extern "C" int mxb_linear_wonly_noalloc(const void* x, int x_dtype, int64_t M, i
 
   mxb::GemvPlan plan = mxb::gemv_plan(M, K, N, bits, kind, block, w_packed, y, x_dtype, x);
   if (!plan.ok) return MXB_E_SHAPE;  // not a split-K (decode) shape
-  // Fewer, longer K splits until the partial sums fit the fixed scratch.
-  const int max_rows = plan.max_krows < kMaxRowsPerSplit ? plan.max_krows : kMaxRowsPerSplit;
+  // Fewer, longer K splits (up to the longest the planned kernel takes)
+  // until the partial sums fit the fixed scratch.
+  const int max_rows = plan.max_krows;
   while (plan.ws_bytes > kScratchBytes && plan.krows < max_rows) {
     int64_t krows = plan.krows * 2 > max_rows ? max_rows : plan.krows * 2;
     plan.krows = (int)krows;

@@ -250,11 +250,14 @@ def _mx_mm(a, b) -> mx_tensor:
     reg = _REGISTRY.find("torch.matmul", a._mx_dtype.name, ARCH)
     if reg is not None and reg.force == "true":
         return _mm_fallback(a, b, out_dt)
+    # Every 2-D pair takes the packed GEMM, whatever the kind or variant
+    # (mxtorch.py:6534-6540 -> 5563-5573): the reference unpacks both
+    # operands' raw codes with A's width, sign-extended (float4d grid
+    # indices 8..15 become -8..-1), and runs _qscale_matmul on them.  The
+    # kernels take codes of one width for both operands.
     is_2d = len(a._mx_orig_shape) == 2 and len(b._mx_orig_shape) == 2
-    same = (a._mx_dtype.bits == b._mx_dtype.bits and a._mx_block == b._mx_block
-            and a._mx_dtype.is_int and b._mx_dtype.is_int
-            and a._mx_dtype.variant in ("", "h") and b._mx_dtype.variant in ("", "h"))
-    if is_2d and same and a._mx_dtype.bits in (1, 2, 4, 8):
+    if (is_2d and a._mx_dtype.bits == b._mx_dtype.bits and a._mx_dtype.bits in (1, 2, 4, 8)
+            and out_dt.bits in (2, 4, 8, 16)):
         return _dispatch_qgemm(a, b, out_dt)
     return _mm_fallback(a, b, out_dt)
 
@@ -266,7 +269,7 @@ def _dispatch_qgemm(a: mx_tensor, b: mx_tensor, out_dt: mx_dtype) -> mx_tensor:
     if K != K2:
         raise ValueError(f"GEMM shape mismatch: {tuple(a._mx_orig_shape)} @ "
                          f"{tuple(b._mx_orig_shape)}")
-    block = a._mx_block
+    block = a._mx_block  # B's scales are viewed [K/block, N] with A's block, as there
     c_packed, c_scales, _ = ops.qgemm(a._mx_packed, a._mx_scales, b._mx_packed, b._mx_scales,
                                       M, K, N, a._mx_dtype.bits, block, out_dt.bits)
     return mx_tensor(c_packed, c_scales, out_dt, torch.Size([M, N]), M * N, block)

@@ -75,6 +75,13 @@ GEMM_CASES = [
     {"key": "g_int2d_b64", "dtype": "int2d", "block": 64, "M": 64, "K": 128, "N": 64, "seed": 35},
     {"key": "g_int1d_b32", "dtype": "int1d", "block": 32, "M": 32, "K": 64, "N": 32, "seed": 36},
     {"key": "g_int8d_ragged", "dtype": "int8d", "block": 128, "M": 16, "K": 200, "N": 48, "seed": 37},
+    # float-kind and variant operands: the reference multiplies their raw
+    # sign-extended codes like int codes (mxtorch.py:5563-5573)
+    {"key": "g_float4d_128x256x128", "dtype": "float4d", "block": 128, "M": 128, "K": 256, "N": 128, "seed": 38},
+    {"key": "g_float4d_ragged", "dtype": "float4d", "block": 128, "M": 16, "K": 200, "N": 48, "seed": 39},
+    {"key": "g_int4dh_128x256x128", "dtype": "int4dh", "block": 128, "M": 128, "K": 256, "N": 128, "seed": 46},
+    {"key": "g_int4d_x_float4d", "dtype": "int4d", "dtype_b": "float4d", "block": 128, "M": 64, "K": 128, "N": 64, "seed": 47},
+    {"key": "g_int2dh_b64", "dtype": "int2dh", "block": 64, "M": 64, "K": 128, "N": 64, "seed": 48},
 ]
 
 

@@ -74,13 +74,14 @@ def main(ref_dir: str) -> None:
         a, b = cases.make_gemm_inputs(c)
         dt = mx.get_mx_dtype(c["dtype"])
         qa = mx.mx_tensor.quantize(a, dt, c["block"])
-        qb = mx.mx_tensor.quantize(b, dt, c["block"])
+        qb = mx.mx_tensor.quantize(b, mx.get_mx_dtype(c.get("dtype_b", c["dtype"])), c["block"])
         qc = qa @ qb
         key = c["key"]
         put(f"{key}/c_packed", qc._mx_packed)
         put(f"{key}/c_scales", qc._mx_scales)
         put(f"{key}/c_bits", np.int64(qc._mx_dtype.bits))
         put(f"{key}/c_block", np.int64(qc._mx_block))
+        put(f"{key}/c_dtype", np.array(qc._mx_dtype.name))
         put(f"{key}/c_dequant", qc.dequantize())
 
     # weight-only linear (mx_linear.from_linear + forward, bias-free)

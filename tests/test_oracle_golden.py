@@ -64,10 +64,18 @@ def test_h_dequant_1d_equals_reference_literal(golden):
 @pytest.mark.parametrize("c", cases.GEMM_CASES, ids=lambda c: c["key"])
 def test_qscale_matmul_matches_reference(golden, c):
     dt = get_mx_dtype(c["dtype"])
+    dtb = get_mx_dtype(c.get("dtype_b", c["dtype"]))
     a, b = cases.make_gemm_inputs(c)
     M, K, N, blk = c["M"], c["K"], c["N"], c["block"]
-    pa, sa, _ = O.quantize(_np(a), dt.bits, dt.kind, blk)
-    pb, sb, _ = O.quantize(_np(b), dt.bits, dt.kind, blk)
+
+    def q(x, d):
+        signs = None
+        if d.is_hadamard:
+            signs = sign_vector(x.shape[-1], d.hadamard_seed).numpy()
+        return O.quantize(_np(x), d.bits, d.kind, blk, hadamard=d.is_hadamard, signs=signs)
+
+    pa, sa, _ = q(a, dt)
+    pb, sb, _ = q(b, dtb)
     ca = O.unpack(pa, dt.bits, M * K)
     cb = O.unpack(pb, dt.bits, K * N)
     out_bits = int(golden[f"{c['key']}/c_bits"])

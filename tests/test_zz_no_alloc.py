@@ -31,8 +31,12 @@ def _noalloc(x, w, N, dt):
     return y
 
 
+# The last case goes through the CUDA-core GEMV (float4 codes) whose own
+# plan, 52 K splits of 80 rows, needs 36 MiB of partial sums: the entry point
+# must lengthen the splits (to 256 rows, 11.3 MiB) to fit its 16 MiB array.
 @pytest.mark.parametrize("M,K,N,dt", [(1, 4096, 11008, "int4d"), (16, 4096, 11008, "int4d"),
-                                      (3, 512, 768, "int8d"), (5, 256, 384, "float4d")])
+                                      (3, 512, 768, "int8d"), (5, 256, 384, "float4d"),
+                                      (16, 4096, 11008, "float4d")])
 def test_noalloc_matches_workspace_path(M, K, N, dt):
     d = mxb.get_mx_dtype(dt)
     g = torch.Generator().manual_seed(M + K)
@@ -46,6 +50,28 @@ def test_noalloc_matches_workspace_path(M, K, N, dt):
         bound = x.float().abs() @ wdq.abs()
         err = (y - ref).abs()
         assert torch.all(err <= LIN_TOL * bound + 1e-30), (call, float((err / bound).max()))
+        # and against float64 x @ dequant(W^T) on sampled columns
+        cols = torch.arange(0, N, max(1, N // 97), device=x.device)
+        y64 = x.double() @ wdq[:, cols].double()
+        err64 = (y[:, cols].double() - y64).abs()
+        assert torch.all(err64 <= LIN_TOL * bound[:, cols].double() + 1e-30), call
+
+
+def test_noalloc_rejects_partials_beyond_the_array():
+    """float4d M=16, K=8192, N=32768: even 256-row K splits need 32 x 16 x
+    32768 x 4 bytes = 64 MiB of partial sums, more than the 16 MiB array, so
+    the call returns MXB_E_WORKSPACE (-7) before launching anything (the
+    buffers are small stand-ins: nothing is read or written)."""
+    w = torch.zeros(1 << 20, dtype=torch.int8, device="cuda")
+    s = torch.ones(1 << 16, device="cuda")
+    x = torch.zeros(16, 8192, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(1 << 16, device="cuda")
+    n0 = L.load().mxb_launch_count()
+    rc = L.load().mxb_linear_wonly_noalloc(L.ptr(x), L.BF16, 16, 8192, L.ptr(w), L.ptr(s),
+                                           32768, 4, L.KIND_FLOAT, 128, L.ptr(y),
+                                           L.stream_of(x.device))
+    assert rc == -7
+    assert L.load().mxb_launch_count() == n0
 
 
 def test_noalloc_rejects_non_gemv_shapes():
