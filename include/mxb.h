@@ -152,6 +152,17 @@ int mxb_dequantize_silu_mul(const void* gate_packed, const float* gate_scales,
 int mxb_hadamard_rows(const float* x, int64_t rows, int64_t d, const float* signs,
                       int inverse, float* out, void* stream);
 
+/* Cross-shard stage of a row WHT split over G column shards (G = 1, 2, 4
+ * or 8), fused with the reorder of the gathered shards.  N = G * L columns,
+ * column j = g * L + l; H_N = H_G (x) H_L.  `t` is the all-gather
+ * [G][M][L] of each rank's t_g = WHT_L(y_g) / sqrt(L) (mxb_hadamard_rows
+ * with unit signs); out[m][g*L + l] = (sum_h H_G[g, h] t_h[m][l]) / sqrt(G)
+ * * signs[g*L + l], i.e. `hadamard_rotation.unrotate` of the full rows
+ * (mxtorch.py:2892-2904) up to fp32 rounding order.  L % 4 == 0, pointers
+ * 16-byte aligned.  No counterpart in the reference (it has no sharding). */
+int mxb_hadamard_cross(const float* t, int64_t M, int64_t L, int G, const float* signs,
+                       float* out, void* stream);
+
 /* Workspace bytes for mxb_qgemm. */
 size_t mxb_qgemm_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int block);
 
@@ -261,6 +272,24 @@ int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const voi
                      const float* w_scales, int64_t N, int bits, int kind, int block,
                      int mode, float* y, void* workspace, size_t workspace_bytes,
                      void* stream);
+
+/*
+ * Weight-only linear with the weight stored K-major: y = x @ dequant(W)^T,
+ * fp32 output.  Replaces the matmul of `mx_dynamic_linear.forward`
+ * (mxtorch.py:8947-8978: tokens.float() @ w_mx.dequantize().t()), whose
+ * weight is W [N = out, K = in] quantized flat along K (`mx_tensor.quantize(
+ * linear.weight)`, 8929-8930), so element (n, k) has scale
+ * w_scales[(n * K + k) / block].  No dequantized weight is materialised.
+ *   x        [M, K] of x_dtype (MXB_F32 / MXB_BF16)
+ *   w_packed / w_scales  the mx_tensor storage of W [N, K]
+ *   y        [M, N] fp32
+ * bf16 x with M > 16, K % 64 == 0, N % 128 == 0, K % block == 0 and 2-8 bit
+ * codes runs the tcgen05 kernel (parity / fast modes as mxb_linear_wonly);
+ * every other shape a CUDA-core kernel.  No workspace.
+ */
+int mxb_linear_wonly_kmajor(const void* x, int x_dtype, int64_t M, int64_t K,
+                            const void* w_packed, const float* w_scales, int64_t N, int bits,
+                            int kind, int block, int mode, float* y, void* stream);
 
 /*
  * The decode (small-M) weight-only linear of mxb_linear_wonly, for callers

@@ -62,6 +62,9 @@ PROTOTYPES = {
     "mxb_linear_wonly_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int, _int]),
     "mxb_linear_wonly": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _i64, _int, _int, _int, _int,
                                 _vp, _vp, _sz, _vp]),
+    "mxb_hadamard_cross": (_int, [_vp, _i64, _i64, _int, _vp, _vp, _vp]),
+    "mxb_linear_wonly_kmajor": (_int, [_vp, _int, _i64, _i64, _vp, _vp, _i64, _int, _int, _int,
+                                       _int, _vp, _vp]),
 }
 
 _lib = None

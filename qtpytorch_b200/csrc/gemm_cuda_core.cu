@@ -98,7 +98,9 @@ __global__ void __launch_bounds__(256) qgemm_generic_kernel(
 }
 
 // ── weight-only GEMM, any shape (fp32 FMA) ───────────────────────────────────
-template <int BITS, int KIND, typename XT>
+// KMAJ: the weight is W [N, K] quantized flat (element (k, n) at n * K + k,
+// the layout of mx_dynamic_linear's weight) instead of W^T [K, N].
+template <int BITS, int KIND, bool KMAJ, typename XT>
 __global__ void __launch_bounds__(256) wonly_generic_kernel(
     const XT* __restrict__ x, int M, int K, const uint8_t* __restrict__ W,
     const float* __restrict__ ws, int N, int block, float* __restrict__ y) {
@@ -119,7 +121,7 @@ __global__ void __launch_bounds__(256) wonly_generic_kernel(
       Xs[kk][c] = (k < K && m < M) ? load_as_f32(x, (int64_t)m * K + k) : 0.0f;
       float w = 0.0f;
       if (k < K && n < N) {
-        int64_t e = (int64_t)k * N + n;
+        const int64_t e = KMAJ ? (int64_t)n * K + k : (int64_t)k * N + n;
         uint32_t raw;
         if constexpr (BITS == 8) {
           raw = __ldg(W + e);
@@ -178,18 +180,19 @@ int qgemm_generic(const void* a, const float* sa, bool sa_ok, const void* b, con
   return MXB_OK;
 }
 
-template <typename XT>
+template <bool KMAJ, typename XT>
 static int wonly_generic_t(const XT* x, int64_t M, int64_t K, const uint8_t* W, const float* ws,
                            int64_t N, int bits, int kind, int block, float* y, cudaStream_t st) {
   dim3 grid((unsigned)cdiv(N, GT), (unsigned)cdiv(M, GT));
+  const int iM = (int)M, iK = (int)K, iN = (int)N;
   if (kind == MXB_KIND_FLOAT) {
-    wonly_generic_kernel<4, MXB_KIND_FLOAT, XT><<<grid, 256, 0, st>>>(x, (int)M, (int)K, W, ws, (int)N, block, y);
+    wonly_generic_kernel<4, MXB_KIND_FLOAT, KMAJ, XT><<<grid, 256, 0, st>>>(x, iM, iK, W, ws, iN, block, y);
   } else {
     switch (bits) {
-      case 1: wonly_generic_kernel<1, MXB_KIND_INT, XT><<<grid, 256, 0, st>>>(x, (int)M, (int)K, W, ws, (int)N, block, y); break;
-      case 2: wonly_generic_kernel<2, MXB_KIND_INT, XT><<<grid, 256, 0, st>>>(x, (int)M, (int)K, W, ws, (int)N, block, y); break;
-      case 4: wonly_generic_kernel<4, MXB_KIND_INT, XT><<<grid, 256, 0, st>>>(x, (int)M, (int)K, W, ws, (int)N, block, y); break;
-      case 8: wonly_generic_kernel<8, MXB_KIND_INT, XT><<<grid, 256, 0, st>>>(x, (int)M, (int)K, W, ws, (int)N, block, y); break;
+      case 1: wonly_generic_kernel<1, MXB_KIND_INT, KMAJ, XT><<<grid, 256, 0, st>>>(x, iM, iK, W, ws, iN, block, y); break;
+      case 2: wonly_generic_kernel<2, MXB_KIND_INT, KMAJ, XT><<<grid, 256, 0, st>>>(x, iM, iK, W, ws, iN, block, y); break;
+      case 4: wonly_generic_kernel<4, MXB_KIND_INT, KMAJ, XT><<<grid, 256, 0, st>>>(x, iM, iK, W, ws, iN, block, y); break;
+      case 8: wonly_generic_kernel<8, MXB_KIND_INT, KMAJ, XT><<<grid, 256, 0, st>>>(x, iM, iK, W, ws, iN, block, y); break;
       default: return MXB_E_DTYPE;
     }
   }
@@ -199,13 +202,18 @@ static int wonly_generic_t(const XT* x, int64_t M, int64_t K, const uint8_t* W, 
 
 int wonly_generic(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
                   const float* ws, int64_t N, int bits, int kind, int block, float* y,
-                  cudaStream_t st) {
+                  cudaStream_t st, bool kmajor) {
   const uint8_t* W = static_cast<const uint8_t*>(w);
-  if (x_dtype == MXB_F32)
-    return wonly_generic_t(static_cast<const float*>(x), M, K, W, ws, N, bits, kind, block, y, st);
-  if (x_dtype == MXB_BF16)
-    return wonly_generic_t(static_cast<const __nv_bfloat16*>(x), M, K, W, ws, N, bits, kind,
-                           block, y, st);
+  if (x_dtype == MXB_F32) {
+    const float* xf = static_cast<const float*>(x);
+    return kmajor ? wonly_generic_t<true>(xf, M, K, W, ws, N, bits, kind, block, y, st)
+                  : wonly_generic_t<false>(xf, M, K, W, ws, N, bits, kind, block, y, st);
+  }
+  if (x_dtype == MXB_BF16) {
+    const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+    return kmajor ? wonly_generic_t<true>(xb, M, K, W, ws, N, bits, kind, block, y, st)
+                  : wonly_generic_t<false>(xb, M, K, W, ws, N, bits, kind, block, y, st);
+  }
   return MXB_E_DTYPE;
 }
 

@@ -210,4 +210,22 @@ int mxb_linear_wonly(const void* x, int x_dtype, int64_t M, int64_t K, const voi
   return wonly_generic(x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y, st);
 }
 
+int mxb_linear_wonly_kmajor(const void* x, int x_dtype, int64_t M, int64_t K,
+                            const void* w_packed, const float* w_scales, int64_t N, int bits,
+                            int kind, int block, int mode, float* y, void* stream) {
+  if (kind == MXB_KIND_FLOAT ? bits != 4 : !int_bits(bits)) return MXB_E_DTYPE;
+  if (kind != MXB_KIND_INT && kind != MXB_KIND_FLOAT) return MXB_E_DTYPE;
+  if (x_dtype != MXB_F32 && x_dtype != MXB_BF16) return MXB_E_DTYPE;
+  if (mode != MXB_MODE_PARITY && mode != MXB_MODE_FAST) return MXB_E_ARG;
+  if (M < 0 || K <= 0 || N <= 0 || block <= 0) return MXB_E_SHAPE;
+  if (M == 0) return MXB_OK;
+  if (M * K >= (int64_t)1 << 31 || K * N >= (int64_t)1 << 31 || M * N >= (int64_t)1 << 31)
+    return MXB_E_SHAPE;
+  if (!x || !w_packed || !w_scales || !y) return MXB_E_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (tc_wonly_eligible(x, x_dtype, M, K, w_packed, N, bits, kind, block, y, /*kmajor*/ true))
+    return tc_wonly(x, M, K, w_packed, w_scales, N, bits, kind, block, mode, y, st, true);
+  return wonly_generic(x, x_dtype, M, K, w_packed, w_scales, N, bits, kind, block, y, st, true);
+}
+
 }  // extern "C"

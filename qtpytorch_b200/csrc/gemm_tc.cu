@@ -29,6 +29,7 @@ __device__ int g_mxb_device_error = 0;
 #include "tc_ptx.cuh"
 #include "wonly_tc.cuh"
 #include "wonly_dec.cuh"
+#include "gemv_tma.cuh"
 
 namespace mxb {
 
@@ -488,19 +489,25 @@ int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int
 
 // ── weight-only GEMM (wonly_tc.cuh) ──────────────────────────────────────────
 bool tc_wonly_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
-                       int64_t N, int bits, int kind, int block, const float* y) {
+                       int64_t N, int bits, int kind, int block, const float* y, bool kmajor) {
   if (x_dtype != MXB_BF16 || M <= 16) return false;
-  if (K % wo::BK || N % wo::BN || block % 8 || N % block) return false;
+  if (K % wo::BK || N % wo::BN || block % 8) return false;
   if (kind == MXB_KIND_FLOAT ? bits != 4 : !(bits == 1 || bits == 2 || bits == 4 || bits == 8))
     return false;
+  if (kmajor) {
+    // the K-major code box is BK * bits / 8 bytes wide: at least 16
+    if (bits < 2 || K % block) return false;
+  } else if (N % block) {
+    return false;
+  }
   if (((uintptr_t)x | (uintptr_t)w | (uintptr_t)y) & 15) return false;
   return true;
 }
 
-template <int BITS, int KIND, bool FAST>
+template <int BITS, int KIND, bool FAST, bool KMAJ>
 static int wonly_launch(const CUtensorMap& tx, const CUtensorMap& tw, const float* ws, int M,
                         int N, int K, int block, float* y, cudaStream_t st) {
-  auto kern = wo::wonly_tc_kernel<BITS, KIND, FAST>;
+  auto kern = wo::wonly_tc_kernel<BITS, KIND, FAST, KMAJ>;
   MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)wo::kSmemBytes));
   dim3 grid((unsigned)(N / wo::BN), (unsigned)cdiv(M, wo::BM));
@@ -510,31 +517,45 @@ static int wonly_launch(const CUtensorMap& tx, const CUtensorMap& tw, const floa
 }
 
 template <int BITS, int KIND>
-static int wonly_mode(bool fast, const CUtensorMap& tx, const CUtensorMap& tw, const float* ws,
-                      int M, int N, int K, int block, float* y, cudaStream_t st) {
-  return fast ? wonly_launch<BITS, KIND, true>(tx, tw, ws, M, N, K, block, y, st)
-              : wonly_launch<BITS, KIND, false>(tx, tw, ws, M, N, K, block, y, st);
+static int wonly_mode(bool fast, bool kmajor, const CUtensorMap& tx, const CUtensorMap& tw,
+                      const float* ws, int M, int N, int K, int block, float* y,
+                      cudaStream_t st) {
+  if (kmajor) {
+    if constexpr (BITS >= 2)
+      return fast ? wonly_launch<BITS, KIND, true, true>(tx, tw, ws, M, N, K, block, y, st)
+                  : wonly_launch<BITS, KIND, false, true>(tx, tw, ws, M, N, K, block, y, st);
+    return MXB_E_DTYPE;
+  }
+  return fast ? wonly_launch<BITS, KIND, true, false>(tx, tw, ws, M, N, K, block, y, st)
+              : wonly_launch<BITS, KIND, false, false>(tx, tw, ws, M, N, K, block, y, st);
 }
 
 int tc_wonly(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
-             int bits, int kind, int block, int mode, float* y, cudaStream_t st) {
+             int bits, int kind, int block, int mode, float* y, cudaStream_t st, bool kmajor) {
   CUtensorMap tx, tw;
   if (make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, (uint64_t)K, (uint64_t)M, wo::BK,
                    128, CU_TENSOR_MAP_SWIZZLE_128B) != MXB_OK)
     return MXB_E_CUDA;
-  const uint64_t row_bytes = (uint64_t)N * bits / 8;
-  if (make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, row_bytes, (uint64_t)K,
-                   (uint32_t)(wo::BN * bits / 8), wo::BK, CU_TENSOR_MAP_SWIZZLE_NONE) != MXB_OK)
-    return MXB_E_CUDA;
+  if (kmajor) {
+    const uint64_t row_bytes = (uint64_t)K * bits / 8;  // one N row of W [N, K]
+    if (make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, row_bytes, (uint64_t)N,
+                     (uint32_t)(wo::BK * bits / 8), wo::BN, CU_TENSOR_MAP_SWIZZLE_NONE) != MXB_OK)
+      return MXB_E_CUDA;
+  } else {
+    const uint64_t row_bytes = (uint64_t)N * bits / 8;
+    if (make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, row_bytes, (uint64_t)K,
+                     (uint32_t)(wo::BN * bits / 8), wo::BK, CU_TENSOR_MAP_SWIZZLE_NONE) != MXB_OK)
+      return MXB_E_CUDA;
+  }
   const bool fast = mode == MXB_MODE_FAST;
   const int iM = (int)M, iN = (int)N, iK = (int)K;
   if (kind == MXB_KIND_FLOAT)
-    return wonly_mode<4, MXB_KIND_FLOAT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
+    return wonly_mode<4, MXB_KIND_FLOAT>(fast, kmajor, tx, tw, ws, iM, iN, iK, block, y, st);
   switch (bits) {
-    case 1: return wonly_mode<1, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
-    case 2: return wonly_mode<2, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
-    case 4: return wonly_mode<4, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
-    case 8: return wonly_mode<8, MXB_KIND_INT>(fast, tx, tw, ws, iM, iN, iK, block, y, st);
+    case 1: return wonly_mode<1, MXB_KIND_INT>(fast, kmajor, tx, tw, ws, iM, iN, iK, block, y, st);
+    case 2: return wonly_mode<2, MXB_KIND_INT>(fast, kmajor, tx, tw, ws, iM, iN, iK, block, y, st);
+    case 4: return wonly_mode<4, MXB_KIND_INT>(fast, kmajor, tx, tw, ws, iM, iN, iK, block, y, st);
+    case 8: return wonly_mode<8, MXB_KIND_INT>(fast, kmajor, tx, tw, ws, iM, iN, iK, block, y, st);
   }
   return MXB_E_DTYPE;
 }
@@ -599,6 +620,120 @@ int tc_wonly_dec(const void* x, int64_t M, int64_t K, const void* w, const float
     case 8: return dec_mp<8>(tw, xb, ws, iM, iN, iK, block, kc, splits, out, st);
   }
   return MXB_E_DTYPE;
+}
+
+// ── streamed GEMV, M <= 2 (gemv_tma.cuh) ─────────────────────────────────────
+bool tma_gemv_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
+                       int64_t N, int bits, int kind, int block, const float* y) {
+  if (kind != MXB_KIND_INT || (bits != 4 && bits != 8)) return false;
+  if (x_dtype != MXB_F32 && x_dtype != MXB_BF16) return false;
+  if (M < 1 || M > 2 || K < 1 || N < 1) return false;
+  if (cdiv(N, gv::GC) * cdiv(K, gv::BR) >= ((int64_t)1 << 31)) return false;
+  const int cpt = 64 / bits;  // columns of one thread's 8 code bytes
+  if (N % 128 || block % cpt || N % block || gv::GC % block) return false;
+  if (((uintptr_t)w & 15) || ((uintptr_t)y & 3)) return false;
+  return true;
+}
+
+gv::Geometry tma_gemv_geometry(int64_t M, int64_t K, int64_t N, int bits, int block) {
+  gv::Geometry g{};
+  g.G = (int)cdiv(N, gv::GC);
+  g.KB = (int)cdiv(K, gv::BR);
+  g.R = (int64_t)g.G * g.KB;
+  g.spr = gv::GC / block;
+  const int mt = M <= 1 ? 1 : 2;
+  const size_t stage = (size_t)gv::BR * gv::GC * bits / 8;
+  const int phases = bits == 4 ? gv::row_phases<4>() : gv::row_phases<8>();
+  const size_t red = (size_t)(phases / 2) * mt * gv::GC * sizeof(float);
+  // per unit of a run: x and scale rows; keep room for at least 4 stages
+  const size_t per_unit = (size_t)gv::BR * (mt + g.spr) * sizeof(float);
+  const int64_t umax_cap = (int64_t)((gv::kSmemBudget - 4 * stage - red - 1024) / per_unit);
+  int64_t C = kSMs;
+  if (C < g.G) C = g.G;                       // a run spans at most two groups
+  if (C < cdiv(g.R, umax_cap)) C = cdiv(g.R, umax_cap);
+  if (C > g.R) C = g.R;
+  g.C = (int)C;
+  g.umax = (int)cdiv(g.R, C);
+  const size_t fixed = (size_t)g.umax * per_unit + red + 2048;
+  int64_t st = (int64_t)((gv::kSmemBudget - fixed) / (stage + 16));
+  if (st > g.umax) st = g.umax;
+  if (st < 1) st = 1;
+  g.stages = (int)st;
+  size_t a, b, c2, d;
+  g.smem = bits == 4 ? (mt == 1 ? gv::smem_layout<4, 1>(g.stages, g.umax, g.spr, &a, &b, &c2, &d)
+                                : gv::smem_layout<4, 2>(g.stages, g.umax, g.spr, &a, &b, &c2, &d))
+                     : (mt == 1 ? gv::smem_layout<8, 1>(g.stages, g.umax, g.spr, &a, &b, &c2, &d)
+                                : gv::smem_layout<8, 2>(g.stages, g.umax, g.spr, &a, &b, &c2, &d));
+  return g;
+}
+
+size_t tma_gemv_workspace(int64_t M, int64_t K, int64_t N, int bits, int block) {
+  const gv::Geometry g = tma_gemv_geometry(M, K, N, bits, block);
+  return (size_t)g.C * 2 * (M <= 1 ? 1 : 2) * gv::GC * sizeof(float);
+}
+
+template <int BITS, int MT, typename XT>
+static int tma_gemv_launch(const CUtensorMap& tw, const XT* x, const float* ws, int M, int K,
+                           int N, int block, const gv::Geometry& g, float* part, float* y,
+                           cudaStream_t st) {
+  auto kern = gv::gemv_tma_kernel<BITS, MT, XT>;
+  MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)g.smem));
+  kern<<<g.C, gv::kThreads, g.smem, st>>>(tw, x, ws, M, K, N, block, g.KB, g.R, g.stages,
+                                          g.umax, g.spr, part);
+  MXB_LAUNCH_CHECK();
+  // the reduction launches as a programmatic dependent: its CTAs start while
+  // the GEMV runs and wait (griddepcontrol.wait) for its results
+  auto red = gv::gemv_tma_reduce<MT>;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(gv::GC / 256, (unsigned)g.G, (unsigned)M);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, red, (const float*)part, M, N, g.KB, g.R, g.C, y);
+  if (e != cudaSuccess) {  // no programmatic launch here: an ordinary stream-ordered one
+    (void)cudaGetLastError();
+    red<<<cfg.gridDim, cfg.blockDim, 0, st>>>(part, M, N, g.KB, g.R, g.C, y);
+  }
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
+template <int BITS, typename XT>
+static int tma_gemv_mt(const CUtensorMap& tw, const XT* x, const float* ws, int M, int K, int N,
+                       int block, const gv::Geometry& g, float* part, float* y,
+                       cudaStream_t st) {
+  return M <= 1 ? tma_gemv_launch<BITS, 1, XT>(tw, x, ws, M, K, N, block, g, part, y, st)
+                : tma_gemv_launch<BITS, 2, XT>(tw, x, ws, M, K, N, block, g, part, y, st);
+}
+
+int tma_gemv(const void* x, int x_dtype, int64_t M, int64_t K, const void* w, const float* ws,
+             int64_t N, int bits, int block, float* y, float* part, size_t part_bytes,
+             cudaStream_t st) {
+  const gv::Geometry g = tma_gemv_geometry(M, K, N, bits, block);
+  if (part_bytes < (size_t)g.C * 2 * (M <= 1 ? 1 : 2) * gv::GC * sizeof(float))
+    return MXB_E_WORKSPACE;
+  CUtensorMap tw;
+  const uint64_t row_bytes = (uint64_t)N * bits / 8;
+  // 8-byte elements: a box row of GC * bits / 8 bytes is more than the 256
+  // elements a byte-typed box may span
+  if (make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, w, row_bytes / 8, (uint64_t)K,
+                   (uint32_t)(gv::GC * bits / 64), gv::BR, CU_TENSOR_MAP_SWIZZLE_NONE) != MXB_OK)
+    return MXB_E_CUDA;
+  const int iM = (int)M, iK = (int)K, iN = (int)N;
+  if (x_dtype == MXB_BF16) {
+    const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+    return bits == 4 ? tma_gemv_mt<4>(tw, xb, ws, iM, iK, iN, block, g, part, y, st)
+                     : tma_gemv_mt<8>(tw, xb, ws, iM, iK, iN, block, g, part, y, st);
+  }
+  const float* xf = static_cast<const float*>(x);
+  return bits == 4 ? tma_gemv_mt<4>(tw, xf, ws, iM, iK, iN, block, g, part, y, st)
+                   : tma_gemv_mt<8>(tw, xf, ws, iM, iK, iN, block, g, part, y, st);
 }
 
 }  // namespace mxb

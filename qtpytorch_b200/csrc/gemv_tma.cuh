@@ -1,0 +1,331 @@
+// Streamed GEMV for the decode regime of the weight-only linear, M <= 2,
+// int4 / int8 codes (configs[2] M = 1 is its headline case):
+//
+//   y[m, n] = sum_k x[m, k] * fl(code[k, n] * s[k, n / block])   (mxtorch.py:7454-7473)
+//
+// The weight stream is the whole cost (24 MB at 4096 x 11008 int4, under 4 us
+// at HBM speed), so what matters is how many bytes are in flight from the
+// first cycle on.  W^T [K, N] is cut into 1024-column groups and 32-row
+// units, one TMA box each (32 rows x 512 bytes for int4: wide rows, because
+// the box rate, not the byte rate, limits narrow boxes); the G * ceil(K / 32)
+// units are dealt out in contiguous runs, one run per CTA and one CTA per SM
+// (a run may cross from the end of one group into the start of the next).  A
+// producer warp issues every box of its run at kernel start into a ring of
+// shared-memory stages (refilled only when the run is longer than the ring),
+// so the device's whole share of the weight is requested at once; sixteen
+// compute warps consume the boxes as they land.
+//
+// Per row of a box each thread owns 8 code bytes (16 int4 / 8 int8 columns),
+// decodes them exactly (byte permute under exponent 0x4B), forms fl(x * s)
+// once per row and accumulates with packed f32x2 FMA (sum_k fl(x*s) * code:
+// one fp32 rounding per term away from the reference's association, within
+// the 1e-5 bound).  At the end of each group's segment the row phases are
+// added in a fixed order and the CTA writes one partial row [M][1024] for
+// that (CTA, segment); a second kernel, launched as a programmatic dependent
+// of the first, adds each group's partials in CTA order.  Results are
+// deterministic.
+//
+// Included by gemm_tc.cu (shares its device error word and the bounded
+// mbarrier waits).
+#pragma once
+
+namespace mxb {
+namespace gv {
+
+constexpr int GC = 1024;            // columns per group
+constexpr int BR = 32;              // K rows per unit (one TMA box)
+constexpr int kComputeWarps = 16;
+constexpr int kComputeThreads = 32 * kComputeWarps;
+constexpr int kThreads = kComputeThreads + 32;  // + producer warp
+constexpr size_t kSmemBudget = 222 * 1024;
+
+struct Geometry {
+  int G;        // column groups
+  int KB;       // units per group (ceil(K / BR))
+  int64_t R;    // units in all
+  int C;        // CTAs
+  int umax;     // longest run of units of one CTA
+  int stages;   // ring stages
+  int spr;      // scales per row per group (GC / block)
+  size_t smem;  // dynamic shared memory bytes
+};
+
+__host__ __device__ inline int64_t run_start(int64_t c, int64_t R, int64_t C) {
+  return c * R / C;
+}
+
+template <int BITS>
+constexpr int group_bytes() { return GC * BITS / 8; }
+template <int BITS>
+constexpr int row_phases() { return kComputeThreads / (group_bytes<BITS>() / 8); }
+
+// Per-CTA shared memory: ring [stages][BR][GB] codes | x [umax*BR][MT] |
+// scales [umax*BR][spr] | red [P/2][MT][GC] | barriers.
+template <int BITS, int MT>
+__host__ __device__ inline size_t smem_layout(int stages, int umax, int spr, size_t* off_x,
+                                              size_t* off_s, size_t* off_red, size_t* off_bar) {
+  size_t o = (size_t)stages * BR * group_bytes<BITS>();
+  *off_x = o;
+  o += (size_t)umax * BR * MT * sizeof(float);
+  *off_s = o;
+  o += (size_t)umax * BR * spr * sizeof(float);
+  o = (o + 15) & ~(size_t)15;
+  *off_red = o;
+  o += (size_t)(row_phases<BITS>() / 2) * MT * GC * sizeof(float);
+  o = (o + 7) & ~(size_t)7;
+  *off_bar = o;
+  o += (size_t)2 * stages * sizeof(uint64_t);
+  return o + 128;  // alignment slack of the base
+}
+
+// Bounded wait that backs off with __nanosleep between polls, so warps that
+// run ahead of the arriving boxes leave the issue slots to the warps that
+// have data.  Warp-uniform result.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int err_code) {
+  bool ok = mbar_test_wait(bar, parity);
+  if (!__all_sync(0xffffffffu, ok)) {
+    const uint64_t t0 = globaltimer_ns();
+    ok = false;
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+      if (mbar_try_wait(bar, parity)) { ok = true; break; }
+      __nanosleep(64);
+      if ((i & 15) == 15 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    if (!ok) atomicCAS(&g_mxb_device_error, 0, err_code);
+    ok = __all_sync(0xffffffffu, ok);
+  }
+  return ok;
+}
+
+__device__ __forceinline__ void compute_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kComputeThreads) : "memory");
+}
+
+template <int BITS, int MT, typename XT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap_w, const XT* __restrict__ x,
+                    const float* __restrict__ ws, int M, int K, int N, int block, int KB,
+                    int64_t R, int stages, int umax, int spr, float* __restrict__ part) {
+  constexpr int GB = group_bytes<BITS>();
+  constexpr int CH = GB / 8;                 // 8-byte chunks per row
+  constexpr int CPT = 64 / BITS;             // columns per chunk
+  constexpr int P = row_phases<BITS>();      // row phases (8 int4, 4 int8)
+  constexpr int RPT = BR / P;                // rows per thread per unit
+  static_assert(P % 2 == 0 && BR % P == 0, "row phases");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                             ~static_cast<uintptr_t>(127));
+  size_t off_x, off_s, off_red, off_bar;
+  smem_layout<BITS, MT>(stages, umax, spr, &off_x, &off_s, &off_red, &off_bar);
+  uint8_t* ring = smem;
+  float* xs = reinterpret_cast<float*>(smem + off_x);     // [umax*BR][MT]
+  float* ss = reinterpret_cast<float*>(smem + off_s);     // [umax*BR][spr]
+  float* red = reinterpret_cast<float*>(smem + off_red);  // [P/2][MT][GC]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + off_bar);
+  uint64_t* empty = full + stages;
+
+  const int C = gridDim.x, c = blockIdx.x;
+  // unit indices fit 32 bits (the host checks R < 2^31): 32-bit div / mod below
+  const int u0 = (int)run_start(c, R, C), u1 = (int)run_start(c + 1, R, C);
+  const int nu = u1 - u0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kComputeWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  // let the partial-sum reduction kernel start launching (it waits for this
+  // grid's completion before reading anything)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == kComputeWarps) {
+    // ── producer: every box of the run, as fast as the ring allows ──
+    if (lane == 0) {
+      prefetch_tmap(&tmap_w);
+      int issued = 0;
+      for (int i = 0; i < nu; ++i) {
+        const int s = i % stages, round = i / stages;
+        if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, kErrTimeoutEmpty)) break;
+        const int u = u0 + i;
+        const int g = u / KB, rb = u % KB;
+        mbar_expect_tx(&full[s], BR * GB);
+        tma_load_2d(ring + (size_t)s * BR * GB, &tmap_w, &full[s], g * (GB / 8), rb * BR);
+        issued = i + 1;
+      }
+      // No box may still be landing when the CTA exits: wait (bounded) for
+      // the last box of every stage (already complete on the normal path).
+      for (int i = issued > stages ? issued - stages : 0; i < issued; ++i)
+        mbar_wait(&full[i % stages], (i / stages) & 1, kErrTimeoutFull);
+    }
+    return;
+  }
+
+  // ── x and scales of the run's rows (plain loads, in flight with the boxes) ──
+  const int nsb = N / block;
+  for (int i = threadIdx.x; i < nu * BR; i += kComputeThreads) {
+    const int u = u0 + i / BR;
+    const int k = (u % KB) * BR + i % BR;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      xs[i * MT + m] = (k < K && m < M) ? load_as_f32(x, (int64_t)m * K + k) : 0.0f;
+  }
+  for (int i = threadIdx.x; i < nu * BR * spr; i += kComputeThreads) {
+    const int row = i / spr, j = i % spr;
+    const int u = u0 + row / BR;
+    const int g = u / KB, k = (u % KB) * BR + row % BR;
+    const int sc = g * spr + j;
+    ss[i] = (k < K && sc < nsb) ? __ldg(ws + (int64_t)k * nsb + sc) : 0.0f;
+  }
+  compute_bar();  // named barrier over the compute warps only (the producer has left)
+
+  const int t = threadIdx.x;
+  const int ch = t % CH, p = t / CH;
+  const int col0 = ch * CPT;       // first column of this thread in the group
+  const int sj = col0 / block;     // scale slot of this thread's chunk
+  uint64_t acc[MT][CPT / 2];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int q = 0; q < CPT / 2; ++q) acc[m][q] = 0ull;
+
+  int cur_g = u0 / KB;
+  int seg = 0;
+  // Phase sums in a fixed order: red[p] = acc(p) for p < P/2, then
+  // red[p - P/2] += acc(p), then the P/2 rows added in order.
+  auto flush = [&]() {
+    if (p < P / 2) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int q = 0; q < CPT / 2; ++q)
+          *reinterpret_cast<float2*>(red + ((size_t)p * MT + m) * GC + col0 + 2 * q) =
+              unpack2(acc[m][q]);
+    }
+    compute_bar();
+    if (p >= P / 2) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int q = 0; q < CPT / 2; ++q) {
+          float2* r = reinterpret_cast<float2*>(red + ((size_t)(p - P / 2) * MT + m) * GC +
+                                                col0 + 2 * q);
+          const float2 a = *r, b = unpack2(acc[m][q]);
+          *r = make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+        }
+    }
+    compute_bar();
+    float* out = part + ((size_t)c * 2 + seg) * MT * GC;
+    for (int i = t; i < MT * GC; i += kComputeThreads) {
+      const int m = i / GC, col = i % GC;
+      float sum = 0.0f;
+#pragma unroll
+      for (int w = 0; w < P / 2; ++w) sum = __fadd_rn(sum, red[((size_t)w * MT + m) * GC + col]);
+      out[i] = sum;
+    }
+    compute_bar();
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int q = 0; q < CPT / 2; ++q) acc[m][q] = 0ull;
+  };
+
+  // After a wait gives up (its code is in the device error word) the warp
+  // stops waiting but keeps every barrier of the loop, so no warp is left
+  // alone at a named barrier; the outputs are then invalid.
+  bool failed = false;
+  for (int i = 0; i < nu; ++i) {
+    const int g = (u0 + i) / KB;
+    if (g != cur_g) {
+      flush();
+      cur_g = g;
+      seg = 1;
+    }
+    const int s = i % stages, round = i / stages;
+    if (!failed && !mbar_wait_sleep(&full[s], round & 1, kErrTimeoutFull)) failed = true;
+    const uint8_t* box = ring + (size_t)s * BR * GB;
+    uint2 wv[RPT];
+#pragma unroll
+    for (int rr = 0; rr < RPT; ++rr)
+      wv[rr] = *reinterpret_cast<const uint2*>(box + (p + rr * P) * GB + ch * 8);
+#pragma unroll
+    for (int rr = 0; rr < RPT; ++rr) {
+      const int li = i * BR + p + rr * P;
+      const float sc = ss[li * spr + sj];
+      uint64_t code[CPT / 2];
+      decode_word2<BITS>(wv[rr].x, code);
+      decode_word2<BITS>(wv[rr].y, code + CPT / 4);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const float xv = __fmul_rn(xs[li * MT + m], sc);
+        const uint64_t x2 = pack2(xv, xv);
+#pragma unroll
+        for (int q = 0; q < CPT / 2; ++q) acc[m][q] = ffma2(x2, code[q], acc[m][q]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (nu > 0) flush();
+}
+
+// y[m, n] = sum over the CTAs whose runs cover n's group, in CTA order, of
+// their partial rows.  One CTA per (256 columns of a group, row m): its
+// first warp lists the group's contributing (CTA, segment) slots once.
+constexpr int kMaxContrib = 1024;
+
+template <int MT>
+__global__ void __launch_bounds__(256) gemv_tma_reduce(const float* __restrict__ part, int M,
+                                                       int N, int KB, int64_t R, int C,
+                                                       float* __restrict__ y) {
+  __shared__ int slots[kMaxContrib];
+  __shared__ int nslots;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int g = blockIdx.y, m = blockIdx.z;
+  const int64_t gs = (int64_t)g * KB, ge = gs + KB;
+  if (threadIdx.x < 32) {
+    // first CTA whose run holds unit gs
+    int64_t cl = gs * C / R;
+    while (cl > 0 && run_start(cl, R, C) > gs) --cl;
+    while (cl + 1 < C && run_start(cl + 1, R, C) <= gs) ++cl;
+    int n = 0;
+    for (int64_t base = cl; base < C; base += 32) {
+      const int64_t cc = base + threadIdx.x;
+      const int64_t a = cc < C ? run_start(cc, R, C) : ge;
+      const int64_t b = cc < C ? run_start(cc + 1, R, C) : ge;
+      const bool in = cc < C && a < ge && b > a && b > gs;
+      const unsigned mask = __ballot_sync(0xffffffffu, in);
+      if (in) {
+        const int pos = n + __popc(mask & ((1u << threadIdx.x) - 1u));
+        if (pos < kMaxContrib) slots[pos] = (int)(cc * 2 + (a < gs ? 1 : 0));
+      }
+      n += __popc(mask);
+      if (__any_sync(0xffffffffu, cc >= C || a >= ge)) break;
+    }
+    if (threadIdx.x == 0) nslots = n < kMaxContrib ? n : kMaxContrib;
+  }
+  __syncthreads();
+  const int col = blockIdx.x * 256 + threadIdx.x;
+  const int n = g * GC + col;
+  if (n >= N) return;
+  // loads of a batch issued together, then added in slot order
+  const float* base = part + (size_t)m * GC + col;
+  float sum = 0.0f;
+  const int ns = nslots;
+  for (int i0 = 0; i0 < ns; i0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = i0 + j < ns ? __ldcg(base + (size_t)slots[i0 + j] * MT * GC) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (i0 + j < ns) sum = __fadd_rn(sum, v[j]);
+  }
+  y[(int64_t)m * N + n] = sum;
+}
+
+}  // namespace gv
+}  // namespace mxb

@@ -140,6 +140,31 @@ __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   return d;
 }
 
+// 32 bits of int4 / int8 codes -> 16/BITS exact float pairs (columns 2p,
+// 2p+1): the offset-binary code u (sign bit flipped) placed under exponent
+// byte 0x4B reads as 2^23 + u, and one packed subtract removes the offset.
+template <int BITS>
+__device__ __forceinline__ void decode_word2(uint32_t w, uint64_t* out) {
+  if constexpr (BITS == 4) {
+    const uint32_t v = w ^ 0x88888888u;  // two's complement -> offset binary (code + 8)
+    const uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
+    const uint64_t bias = pack2(8388616.0f, 8388616.0f);  // 2^23 + 8
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      out[k] = fsub2(pack2(__int_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + k)),
+                           __int_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + k))),
+                     bias);
+  } else {  // BITS == 8
+    const uint32_t v = w ^ 0x80808080u;  // code + 128
+    const uint64_t bias = pack2(8388736.0f, 8388736.0f);  // 2^23 + 128
+#pragma unroll
+    for (int k = 0; k < 2; ++k)
+      out[k] = fsub2(pack2(__int_as_float(__byte_perm(v, 0x4B000000u, 0x7440 + 2 * k)),
+                           __int_as_float(__byte_perm(v, 0x4B000000u, 0x7441 + 2 * k))),
+                     bias);
+  }
+}
+
 __device__ __forceinline__ float load_as_f32(const float* p, int64_t i) { return __ldg(p + i); }
 __device__ __forceinline__ float load_as_f32(const __nv_bfloat16* p, int64_t i) {
   return __bfloat162float(p[i]);

@@ -16,9 +16,10 @@ namespace mxb {
 int qgemm_generic(const void* a, const float* sa, bool sa_ok, const void* b, const float* sb,
                   bool sb_ok, int64_t M, int64_t K, int64_t N, int bits, int block, float* C,
                   cudaStream_t st);
+// kmajor: the weight is W [N, K] quantized flat instead of W^T [K, N]
 int wonly_generic(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
                   const float* ws, int64_t N, int bits, int kind, int block, float* y,
-                  cudaStream_t st);
+                  cudaStream_t st, bool kmajor = false);
 
 // gemv.cu
 constexpr int kDecMaxKc = 2048;  // K rows per CTA of the tcgen05 decode kernel
@@ -28,14 +29,16 @@ struct GemvPlan {
   int krows;        // rows of K per split
   size_t ws_bytes;  // partial-sum workspace
   int kernel = 0;   // 0: 8 columns per thread, any code width; 1: wide loads (int4/int8);
-                    // 4: tcgen05 decode kernel (bf16 x, integer codes, 3 <= M <= 32)
+                    // 4: tcgen05 decode kernel (bf16 x, integer codes, 3 <= M <= 32);
+                    // 5: streamed TMA GEMV (int4 / int8, M <= 2)
   int lb = 0;       // kernel 1: code bytes per thread and row (4, 8 or 16)
   int max_krows = 0;  // largest rows per split the kernel accepts
 };
 // x_dtype < 0: the dtype is not known yet (workspace queries); the plan then
 // covers the largest workspace either activation dtype may need.
 GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,
-                   const void* w, const void* y, int x_dtype, const void* x);
+                   const void* w, const void* y, int x_dtype, const void* x,
+                   bool allow_tma = true);
 int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_t K,
              const void* w, const float* ws, int64_t N, int bits, int kind, int block,
              float* y, float* partial, cudaStream_t st);
@@ -66,14 +69,24 @@ int transpose_scales(const float* s, int64_t kbn, int64_t N, float* out, cudaStr
 int widen_transpose(const void* bt, int64_t K, int64_t N, int bits, bool pm1, int8_t* out,
                     cudaStream_t st);
 int widen_codes(const void* p, int64_t n, int bits, int8_t* out, bool pm1, cudaStream_t st);
+// kmajor: W [N, K] quantized flat (scale s[n, k / block]) instead of W^T [K, N]
 bool tc_wonly_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
-                       int64_t N, int bits, int kind, int block, const float* y);
+                       int64_t N, int bits, int kind, int block, const float* y,
+                       bool kmajor = false);
 int tc_wonly(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
-             int bits, int kind, int block, int mode, float* y, cudaStream_t st);
+             int bits, int kind, int block, int mode, float* y, cudaStream_t st,
+             bool kmajor = false);
 bool tc_dec_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w, int64_t N,
                      int bits, int kind, int block);
 void tc_dec_plan(int64_t K, int64_t N, int* splits, int* kc);
 int tc_wonly_dec(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
                  int bits, int block, int kc, int splits, float* out, cudaStream_t st);
+// streamed GEMV (M <= 2, int4 / int8 codes): partial rows in `part`
+bool tma_gemv_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
+                       int64_t N, int bits, int kind, int block, const float* y);
+size_t tma_gemv_workspace(int64_t M, int64_t K, int64_t N, int bits, int block);
+int tma_gemv(const void* x, int x_dtype, int64_t M, int64_t K, const void* w, const float* ws,
+             int64_t N, int bits, int block, float* y, float* part, size_t part_bytes,
+             cudaStream_t st);
 
 }  // namespace mxb

@@ -88,12 +88,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <int BITS, int KIND, bool FAST>
+// KMAJ: the weight is W [N, K] quantized flat (mx_dynamic_linear's layout,
+// scale s[n, k / block]); its code tile arrives K-major, [128 N rows][BK
+// codes], which is already the plane's orientation, so the transform reads
+// 8 consecutive K codes of one N row instead of transposing.
+template <int BITS, int KIND, bool FAST, bool KMAJ>
 __global__ void __launch_bounds__(kThreads, 1)
     wonly_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                     const __grid_constant__ CUtensorMap tmap_w, const float* __restrict__ ws,
                     int M, int N, int K, int block, float* __restrict__ y) {
   constexpr int kCodeRow = BN * BITS / 8;     // bytes of one K row of the code tile
+  constexpr int kCodeRowK = BK * BITS / 8;    // KMAJ: bytes of one N row of the code tile
   constexpr int kCodeStage = BK * kCodeRow;
   // parity: per M half one N = 256 accumulator, columns [0, 128) the hi
   // plane's products and [128, 256) the mid plane's (the planes are stored
@@ -146,7 +151,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(&bars->full[s], kAStage + kCodeStage);
         tma_load_2d(sA + s * kAStage, &tmap_x, &bars->full[s], ks * BK, m0);
         tma_load_2d(sA + s * kAStage + kAHalf, &tmap_x, &bars->full[s], ks * BK, m0 + 128);
-        tma_load_2d(sC + s * kCodeStageMax, &tmap_w, &bars->full[s], n0 * BITS / 8, ks * BK);
+        if constexpr (KMAJ)
+          tma_load_2d(sC + s * kCodeStageMax, &tmap_w, &bars->full[s], ks * kCodeRowK, n0);
+        else
+          tma_load_2d(sC + s * kCodeStageMax, &tmap_w, &bars->full[s], n0 * BITS / 8, ks * BK);
       }
     }
   } else if (warp == 1) {
@@ -173,6 +181,99 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&bars->bfree[j]);
       }
       mma_commit(&bars->accfull);
+    }
+  } else if (KMAJ) {
+    // ── transform, K-major codes: thread (n8 = t / 8, k8 = t % 8) takes the
+    // 8 K codes k8*8.. of N rows n8*8 + c, c = 0..7 (row order rotated by
+    // n8 so the warp's four rows sit in different banks) ──
+    const int grp = (warp - 2) >> 2;
+    const int t = (threadIdx.x - 64) & 127;
+    const int n8 = t >> 3, k8 = t & 7;
+    const int nkb = K / block;  // scales per N row (K % block == 0)
+    const float* sp = ws + (size_t)(n0 + n8 * 8) * nkb;
+    float sc_next[8];
+    if (grp < ksteps) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        sc_next[c] = __ldg(sp + (size_t)c * nkb + (grp * BK + k8 * 8) / block);
+    }
+    for (int ks = grp; ks < ksteps; ks += 2) {
+      const int s = ks % STAGES, round = ks / STAGES;
+      const int j = grp, usej = ks >> 1;
+      float sc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) sc[c] = sc_next[c];
+      if (ks + 2 < ksteps) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          sc_next[c] = __ldg(sp + (size_t)c * nkb + ((ks + 2) * BK + k8 * 8) / block);
+      }
+      if (!mbar_wait_warp(&bars->full[s], round & 1, kErrTimeoutFull)) break;
+      uint64_t word[8];
+      const uint8_t* cp = sC + s * kCodeStageMax + k8 * BITS;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int r = n8 * 8 + ((c + n8) & 7);
+        word[c] = lds_codes<BITS>(cp + r * kCodeRowK);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->empty[s]);
+      if (usej > 0 && !mbar_wait_warp(&bars->bfree[j], (usej - 1) & 1, kErrTimeoutTmemEmpty))
+        break;
+      uint8_t* phi = sP + (2 * j) * kPlane;
+      uint8_t* pmid = sP + (2 * j + 1) * kPlane;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int cc = (c + n8) & 7;
+        const int r = n8 * 8 + cc;  // N row of the plane
+        float w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          w[i] = wdeq<BITS, KIND>((uint32_t)(word[c] >> (i * BITS)) & ((1u << BITS) - 1u), sc[cc]);
+        uint4 hv, mv;
+        uint32_t* h4 = reinterpret_cast<uint32_t*>(&hv);
+        uint32_t* m4 = reinterpret_cast<uint32_t*>(&mv);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          h4[p] = bf16x2_rn(w[2 * p], w[2 * p + 1]);
+          if (!FAST)
+            m4[p] = bf16x2_rn(__fsub_rn(w[2 * p], bf16lo_f(h4[p])),
+                              __fsub_rn(w[2 * p + 1], bf16hi_f(h4[p])));
+        }
+        const int off = r * 128 + ((k8 ^ (r & 7)) << 4);  // 128-byte swizzle, K-major
+        *reinterpret_cast<uint4*>(phi + off) = hv;
+        if (!FAST) *reinterpret_cast<uint4*>(pmid + off) = mv;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->bready[j]);
+    }
+    // ── epilogue: TMEM -> y ──
+    if (mbar_wait_warp(&bars->accfull, 0, kErrTimeoutDone)) {
+      tc_fence_after();
+      const int q = warp & 3;
+      const int h = grp;
+      const int m = m0 + h * 128 + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32], rm[32];
+        const uint32_t ta = tbase + ((uint32_t)(q * 32) << 16) + h * kAcc + c * 32;
+        tmem_ld32(ta, r);
+        if (!FAST) tmem_ld32(ta + BN, rm);
+        tmem_wait_ld();
+        if (!FAST) {
+#pragma unroll
+          for (int v = 0; v < 32; ++v)
+            r[v] = __float_as_uint(__fadd_rn(__uint_as_float(r[v]), __uint_as_float(rm[v])));
+        }
+        if (m < M) {
+          float4* o = reinterpret_cast<float4*>(y + (size_t)m * N + n0 + c * 32);
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            o[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+        }
+      }
     }
   } else {
     // ── transform: two groups of 4 warps take alternate K steps, group j

@@ -14,8 +14,9 @@ Mirrors of mxtorch's ``dynamic_quantize`` (mxtorch.py:2665-2712),
   the weight's K-blocks by repeating its scale per block.
 - ``mx_dynamic_linear``: the reference quantizes the activations but its
   output uses the fp32 activations and the dequantized weight (8960-8967),
-  so here the weight is dequantized by the CUDA kernel and multiplied in
-  fp32; the activation codes, which nothing reads, are not computed.
+  so here the packed [out, in] weight goes straight into the K-major
+  weight-only kernel (``mxb_linear_wonly_kmajor``) with the activations as
+  given; the activation codes, which nothing reads, are not computed.
 """
 from __future__ import annotations
 
@@ -82,8 +83,9 @@ def fused_int8_linear(x: mx_tensor, weight: mx_tensor, bias: Optional[torch.Tens
 
     Runs the k-major integer GEMM when x and weight hold base int codes of one
     width whose scale blocks nest (one a multiple of the other, both dividing
-    K); other operands go through the CUDA dequantize and an fp32 matmul,
-    the reference's own CPU formula."""
+    K); otherwise x is dequantized (CUDA kernel) and meets the packed weight
+    in the K-major weight-only kernel, the reference's CPU formula
+    F.linear(dequant(x), dequant(W)) without a dequantized weight."""
     if not isinstance(x, mx_tensor) or not isinstance(weight, mx_tensor):
         raise TypeError("fused_int8_linear takes two mx_tensors")
     K = x._mx_orig_shape[-1] if len(x._mx_orig_shape) >= 2 else x._mx_block
@@ -101,11 +103,25 @@ def fused_int8_linear(x: mx_tensor, weight: mx_tensor, bias: Optional[torch.Tens
         sw = _kblock_scales(weight, N, K, kb)
         _, _, out = ops.qgemm(x._mx_packed, sx, weight._mx_packed, sw, M, K, N, xd.bits, kb,
                               32, b_kmajor=True)
-    else:
+    elif ops.kernel_dtype_ok(wd) and weight._mx_n == N * K:
+        # the dequantized x against the packed weight, read K-major as stored
+        out = _kmajor_linear(x.dequantize().reshape(M, K), weight, K, N)
+    else:  # weight dtype outside the kernels: the reference's formula
         out = F.linear(x.dequantize().reshape(M, K), weight.dequantize().reshape(N, K))
     if bias is not None:
         out = out + bias.to(out.device).float()
     return out
+
+
+def _kmajor_linear(tokens: torch.Tensor, w: mx_tensor, K: int, N: int) -> torch.Tensor:
+    """tokens [M, K] @ dequant(W)^T for W [N, K] quantized flat, on the
+    K-major weight-only kernel.  An ``h`` weight (rotated along K) meets the
+    tokens rotated the same way: x @ unrotate(D)^T = rotate(x) @ D^T."""
+    dt = w._mx_dtype
+    if dt.is_hadamard:
+        tokens = ops.hadamard_rows(tokens.float(), dt.hadamard_seed, inverse=False)
+        dt = dt.base
+    return ops.linear_wonly_kmajor(tokens, w._mx_packed, w._mx_scales, K, N, dt, w._mx_block)
 
 
 class mx_dynamic_linear(nn.Module):
@@ -137,13 +153,24 @@ class mx_dynamic_linear(nn.Module):
         return m
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        x_f = x.dequantize() if isinstance(x, mx_tensor) else x.float()
+        """fp32(x) @ dequant(W)^T + bias (mxtorch.py:8947-8978) on the K-major
+        weight-only kernel: the packed [out, in] weight is read as stored.
+        A bf16 x is passed as is (its fp32 value is exact in bf16); an ``h``
+        weight, rotated along ``in``, meets x rotated the same way, since
+        x @ unrotate(D)^T = rotate(x) @ D^T."""
+        x_f = x.dequantize() if isinstance(x, mx_tensor) else x
+        if x_f.dtype not in (torch.float32, torch.bfloat16):
+            x_f = x_f.float()
         w = self.weight
         if not isinstance(w, mx_tensor):
             w = mx_tensor.quantize(w, self.weight_dtype, self.weight_block)
-        tokens = x_f.reshape(-1, self.in_features).to(w._mx_packed.device)
-        w_dq = w.dequantize().reshape(self.out_features, self.in_features)
-        out = (tokens @ w_dq.t()).reshape(*x_f.shape[:-1], self.out_features)
+        K, N = self.in_features, self.out_features
+        tokens = x_f.reshape(-1, K).to(w._mx_packed.device)
+        if ops.kernel_dtype_ok(w._mx_dtype):
+            out = _kmajor_linear(tokens, w, K, N)
+        else:  # weight dtype outside the kernels: the reference's formula
+            out = tokens.float() @ w.dequantize().reshape(N, K).t()
+        out = out.reshape(*x_f.shape[:-1], N)
         if self.bias is not None:
             out = out + self.bias
         return out

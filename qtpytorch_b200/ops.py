@@ -126,18 +126,38 @@ def dequantize(packed: torch.Tensor, scales: torch.Tensor, dt, n: int, block: in
     return out.reshape(shape)
 
 
-def hadamard_rows(y: torch.Tensor, seed: int, inverse: bool) -> torch.Tensor:
-    """Randomized WHT along the last dim of a fp32 CUDA tensor (in a new tensor)."""
+def hadamard_rows(y: torch.Tensor, seed: Optional[int], inverse: bool) -> torch.Tensor:
+    """Randomized WHT along the last dim of a fp32 CUDA tensor (in a new tensor).
+    ``seed`` None: unit signs (the plain WHT / sqrt(n))."""
     L.require_cuda(y, "hadamard_rows")
     y = y.float().contiguous()
     d = y.shape[-1]
     rows = y.numel() // max(d, 1)
     out = torch.empty_like(y)
-    signs = device_signs(d, seed, y.device)
+    if seed is None:
+        from .hadamard import pow2ceil
+        signs = torch.ones(pow2ceil(d), dtype=torch.float32, device=y.device)
+    else:
+        signs = device_signs(d, seed, y.device)
     with torch.cuda.device(y.device):
         rc = L.load().mxb_hadamard_rows(L.ptr(y), rows, d, L.ptr(signs), int(inverse),
                                         L.ptr(out), L.stream_of(y.device))
     L.check(rc, "mxb_hadamard_rows")
+    return out
+
+
+def hadamard_cross(t: torch.Tensor, M: int, cols: int, G: int, seed: int) -> torch.Tensor:
+    """[M, G*cols] fp32 from the gathered [G, M, cols] per-shard transforms
+    t_g = WHT(y_g)/sqrt(cols): the G-point cross-shard stage, / sqrt(G), times
+    the signs of the full row (mxb_hadamard_cross)."""
+    L.require_cuda(t, "hadamard_cross")
+    t = t.float().contiguous()
+    out = torch.empty(M, G * cols, dtype=torch.float32, device=t.device)
+    signs = device_signs(G * cols, seed, t.device)
+    with torch.cuda.device(t.device):
+        rc = L.load().mxb_hadamard_cross(L.ptr(t), M, cols, G, L.ptr(signs), L.ptr(out),
+                                         L.stream_of(t.device))
+    L.check(rc, f"mxb_hadamard_cross(M={M}, L={cols}, G={G})")
     return out
 
 
@@ -205,6 +225,31 @@ def linear_wonly(x: torch.Tensor, w_packed: torch.Tensor, w_scales: torch.Tensor
                                   dt.bits, _kind(dt), block, mode, L.ptr(y), L.ptr(ws), wsb,
                                   L.stream_of(dev))
     L.check(rc, f"mxb_linear_wonly({M}x{K}x{N}, {dt.name})")
+    return y
+
+
+def linear_wonly_kmajor(x: torch.Tensor, w_packed: torch.Tensor, w_scales: torch.Tensor, K: int,
+                        N: int, dt, block: int, mode: int = L.MODE_PARITY) -> torch.Tensor:
+    """y[M, N] fp32 = x[M, K] @ dequant(W)^T for W [N, K] quantized flat (its
+    blocks run along K): the matmul of mx_dynamic_linear.forward
+    (mxtorch.py:8947-8978) without a dequantized weight.  Base dtypes."""
+    dt = get_mx_dtype(dt)
+    _check_dtype(dt)
+    if dt.is_hadamard:
+        raise NotImplementedError("linear_wonly_kmajor takes base dtypes (rotate x for 'h')")
+    L.require_cuda(w_packed, "linear_wonly_kmajor")
+    dev = w_packed.device
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float()
+    x = x.to(dev).contiguous()
+    M = x.numel() // K
+    y = torch.empty(M, N, dtype=torch.float32, device=dev)
+    in_t = L.BF16 if x.dtype == torch.bfloat16 else L.F32
+    with torch.cuda.device(dev):
+        rc = L.load().mxb_linear_wonly_kmajor(L.ptr(x), in_t, M, K, L.ptr(w_packed),
+                                              L.ptr(w_scales.contiguous()), N, dt.bits,
+                                              _kind(dt), block, mode, L.ptr(y), L.stream_of(dev))
+    L.check(rc, f"mxb_linear_wonly_kmajor({M}x{K}x{N}, {dt.name})")
     return y
 
 

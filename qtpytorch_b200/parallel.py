@@ -229,6 +229,13 @@ class ShardedLinearWeight:
         nsb = N // self.block
         self.scales = (w._mx_scales[: K * nsb].view(K, nsb)
                        [:, n0 // self.block: n1 // self.block].contiguous())
+        # ``h`` rows unrotate as local L-point transforms plus one G-point
+        # stage across the shards when every shard has the same power-of-two
+        # width L and N = G * L is a power of two (the Kronecker split)
+        widths = {b - a for a, b in self.shards}
+        L_ = n1 - n0
+        self.kron_split = (self.dtype.is_hadamard and len(widths) == 1 and world in (1, 2, 4, 8)
+                           and L_ & (L_ - 1) == 0 and L_ % 4 == 0)
 
     @classmethod
     def from_module(cls, m, world: int, rank: int) -> "ShardedLinearWeight":
@@ -253,6 +260,18 @@ def sharded_linear(x: torch.Tensor, w: ShardedLinearWeight, group=None, mode: st
     md = L.MODE_FAST if mode == "fast" else L.MODE_PARITY
     y = ops.linear_wonly(xm, w.codes, w.scales, K, w.n1 - w.n0, w.dtype, w.block, md)
     h = w.dtype.is_hadamard
+    if h and w.kron_split:
+        # H_N = H_G (x) H_L: each rank transforms its own L columns, the one
+        # all-gather moves those, and one kernel runs the G-point stage, the
+        # signs and the reorder to row-major
+        L_ = w.n1 - w.n0
+        t = ops.hadamard_rows(y, None, inverse=True)
+        if w.world > 1:
+            t = _all_gather(t.contiguous(), w.world, group)  # [G, M, L]
+        y = ops.hadamard_cross(t, M, L_, w.world, w.dtype.hadamard_seed)
+        if out_dtype == torch.bfloat16:
+            y = y.bfloat16()
+        return y.reshape(*lead, w.N)
     if out_dtype == torch.bfloat16 and not h:
         y = y.bfloat16()
     if w.world > 1:
@@ -321,14 +340,46 @@ def gather_columns(c_packed: torch.Tensor, c_scales: torch.Tensor, M: int, world
 def sharded_quantize(x: torch.Tensor, dt, block: int, world: int, rank: int):
     """Row-sharded quantize: this rank's (packed, scales) for its block range of
     the flattened tensor, with no communication.  Concatenating the ranks'
-    outputs in rank order gives exactly ``ops.quantize(x)``."""
+    outputs in rank order gives exactly ``ops.quantize(x)``.
+
+    ``h`` dtypes rotate whole rows of the last dim (mxtorch.py:1720-1736), so
+    their shards are whole rows, in units of the fewest rows that also end on
+    a block boundary (lcm(row, block) elements); the returned range is then
+    in blocks as well."""
     from .dtypes import get_mx_dtype
     dt = get_mx_dtype(dt)
     if dt.is_hadamard:
-        raise NotImplementedError("row sharding of 'h' dtypes needs whole rows per rank")
+        return _sharded_quantize_rows(x, dt, block, world, rank)
     flat = x.reshape(-1)
     nb = -(-flat.numel() // block)
     b0, b1 = row_shard(nb, world, rank)
     part = flat[b0 * block: min(b1 * block, flat.numel())]
     packed, scales, _ = ops.quantize(part, dt, block)
     return packed, scales, (b0, b1)
+
+
+def h_row_range(shape, block: int, bits: int, world: int, rank: int) -> Tuple[int, int]:
+    """Rows [r0, r1) of an ``h`` tensor's last-dim rows held by ``rank``: whole
+    rows, in units of lcm(row, block) elements so every shard starts on a
+    block (and byte) boundary."""
+    import math
+    d = ops.row_len_of(shape)
+    n = 1
+    for s in shape:
+        n *= int(s)
+    rows = n // d if d else 0
+    unit = math.lcm(d, block) // d  # rows per unit: whole rows ending on a block boundary
+    if (unit * d * bits) % 8:
+        raise ValueError("row shards of this width do not end on a whole byte")
+    u0, u1 = row_shard(-(-rows // unit), world, rank)
+    return min(u0 * unit, rows), min(u1 * unit, rows)
+
+
+def _sharded_quantize_rows(x: torch.Tensor, dt, block: int, world: int, rank: int):
+    d = ops.row_len_of(x.shape)
+    rows = x.numel() // d if d else 0
+    r0, r1 = h_row_range(x.shape, block, dt.bits, world, rank)
+    part = x.reshape(rows, d)[r0:r1]
+    packed, scales, _ = ops.quantize(part, dt, block)
+    b0 = r0 * d // block
+    return packed, scales, (b0, b0 + scales.numel())

@@ -228,3 +228,91 @@ def test_sharded_qgemm_uneven_shards():
                                    M, K, N, 128, 16)
     assert np.array_equal(words, O.pack(codes, 16))
     assert np.array_equal(scales.view(np.uint32), cs.view(np.uint32))
+
+
+# ── Kronecker split of the h unrotation over column shards ──
+
+def _cross_stage(t, signs):
+    """numpy stand-in for mxb_hadamard_cross: t [G, M, L] -> [M, G*L]."""
+    G = t.shape[0]
+    v = [t[g].astype(np.float32) for g in range(G)]
+    h = G // 2
+    while h >= 1:
+        for g in range(G):
+            if g & h:
+                continue
+            e, o = v[g], v[g + h]
+            v[g], v[g + h] = (e + o).astype(np.float32), (e - o).astype(np.float32)
+        h //= 2
+    z = np.concatenate([(vg / np.float32(np.sqrt(G))).astype(np.float32) for vg in v], axis=1)
+    return (z * signs[None, :]).astype(np.float32)
+
+
+def _kron_rank(rank, port, world, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from qtpytorch_b200.dtypes import get_mx_dtype
+        from qtpytorch_b200.hadamard import sign_vector
+        dt = get_mx_dtype("int4dh")
+        M, N = 5, 1024
+        y = np.random.default_rng(5).standard_normal((M, N)).astype(np.float32)
+        L = N // world
+        # this rank's local stage: the plain normalized WHT of its columns
+        t = torch.from_numpy(O.fwht(y[:, rank * L:(rank + 1) * L]))
+        g = P._all_gather(t.contiguous(), world, None)  # [G, M, L], as NCCL lays it out
+        z = _cross_stage(g.numpy(), sign_vector(N, dt.hadamard_seed).numpy())
+        if rank == 0:
+            result_q.put(z)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_kronecker_split_unrotation(world):
+    """Local L-point transforms + one gather + the G-point stage equal the
+    full-row unrotation (mxtorch.py:2892-2904) to fp32 rounding."""
+    from qtpytorch_b200.dtypes import get_mx_dtype
+    from qtpytorch_b200.hadamard import sign_vector
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_kron_rank, args=(r, port, world, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    z = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    y = np.random.default_rng(5).standard_normal((5, 1024)).astype(np.float32)
+    ref = O.unrotate(y, sign_vector(1024, get_mx_dtype("int4dh").hadamard_seed).numpy())
+    bound = np.abs(y).astype(np.float64).sum(axis=1, keepdims=True) / np.sqrt(1024)
+    assert np.all(np.abs(z.astype(np.float64) - ref) <= 1e-6 * bound)
+
+
+@pytest.mark.parametrize("shape,block,world", [((12, 256), 128, 3), ((7, 96), 64, 2),
+                                               ((5, 100), 128, 2), ((300,), 64, 2)])
+def test_h_row_sharded_quantize_concatenates_to_full(shape, block, world):
+    """Row-sharded quantize of an h dtype: whole rows per rank (rotation is per
+    row), shard starts on block boundaries; concatenation = full quantize."""
+    from qtpytorch_b200.dtypes import get_mx_dtype
+    from qtpytorch_b200.hadamard import sign_vector
+    dt = get_mx_dtype("int4dh")
+    x = np.random.default_rng(9).standard_normal(shape).astype(np.float32)
+    d = shape[-1] if len(shape) >= 2 else x.size
+    signs = sign_vector(d, dt.hadamard_seed).numpy()
+    full_p, full_s, _ = O.quantize(x, 4, "int", block, True, signs)
+    rows = x.reshape(-1, d)
+    ps, ss, got_rows = [], [], 0
+    for r in range(world):
+        r0, r1 = P.h_row_range(shape, block, 4, world, r)
+        assert r0 == got_rows
+        got_rows = r1
+        if r1 > r0:
+            part = rows[r0:r1] if len(shape) >= 2 else rows[r0:r1].reshape(-1)
+            p, s, _ = O.quantize(part, 4, "int", block, True, signs)
+            ps.append(p)
+            ss.append(s)
+    assert got_rows == rows.shape[0]
+    assert np.array_equal(np.concatenate(ps), full_p)
+    assert np.array_equal(np.concatenate(ss), full_s)

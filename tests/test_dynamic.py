@@ -130,3 +130,72 @@ def test_mx_dynamic_linear(golden_dynamic, c):
         mag = mag + np.abs(lin.bias.detach().numpy())[None, :]
     assert np.all(np.abs(out - ref) <= LIN_TOL * mag)
     assert np.all(np.abs(out - g[f"{key}/out"]) <= 2 * LIN_TOL * mag)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,N,dt,x_dt,block", [
+    (64, 512, 256, "int4d", torch.bfloat16, 128),    # tcgen05, K-major codes
+    (300, 1024, 384, "int8d", torch.bfloat16, 64),   # tcgen05, ragged M tile
+    (40, 256, 128, "int2d", torch.bfloat16, 128),    # tcgen05, 2-bit
+    (48, 512, 256, "float4d", torch.bfloat16, 128),  # tcgen05, grid codes
+    (7, 384, 96, "int4d", torch.float32, 128),       # CUDA-core kernel
+    (33, 200, 72, "int1d", torch.bfloat16, 8),       # CUDA-core: 1-bit, blocks across rows
+    (5, 256, 64, "int4dh", torch.float32, 128),      # h weight: rotated x
+])
+def test_linear_wonly_kmajor(M, K, N, dt, x_dt, block):
+    """y = x @ dequant(W)^T for W [N, K] quantized flat along K, without a
+    dequantized weight (mx_dynamic_linear's matmul, mxtorch.py:8947-8978)."""
+    from qtpytorch_b200 import dynamic as D
+    d = mxb.get_mx_dtype(dt)
+    g = torch.Generator().manual_seed(M * 7 + K)
+    w = torch.randn(N, K, generator=g) * 0.02
+    x = torch.randn(M, K, generator=g).to(x_dt)
+    q = mxb.mx_tensor.quantize(w.cuda(), d, block)
+    n0 = mxb._lib.load().mxb_launch_count()
+    y = D._kmajor_linear(x.cuda(), q, K, N).cpu().numpy().astype(np.float64)
+    assert mxb._lib.load().mxb_launch_count() > n0
+    assert mxb._lib.load().mxb_device_error(1) == 0
+    w_dq = q.dequantize().cpu().numpy().reshape(N, K).astype(np.float64)
+    xf = x.float().numpy().astype(np.float64)
+    ref, mag = xf @ w_dq.T, np.abs(xf) @ np.abs(w_dq).T
+    if d.is_hadamard:  # rotation error of x enters through |rotate(x)| @ |D|
+        D_rot = mxb.ops.dequantize(q._mx_packed, q._mx_scales, d.base, q._mx_n, block,
+                                   (N, K)).cpu().numpy().astype(np.float64)
+        xr = mxb.ops.hadamard_rows(x.float().cuda(), d.hadamard_seed, False).cpu().numpy()
+        mag = np.abs(xr.astype(np.float64)) @ np.abs(D_rot).T
+    assert np.all(np.abs(y - ref) <= LIN_TOL * mag + 1e-30), float(np.max(np.abs(y - ref) / mag))
+
+
+@pytest.mark.gpu
+def test_mx_dynamic_linear_prefill_bf16():
+    """bf16 tokens at a prefill size go to the tcgen05 K-major kernel."""
+    lin = torch.nn.Linear(512, 384, bias=True)
+    g = torch.Generator().manual_seed(77)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(384, 512, generator=g) * 0.02)
+        lin.bias.copy_(torch.randn(384, generator=g) * 0.1)
+    m = mxb.mx_dynamic_linear.from_linear(lin, "int4d", "int8d")
+    x = torch.randn(2, 96, 512, generator=g).bfloat16()
+    out = m(x.cuda()).cpu().numpy().astype(np.float64)
+    w_dq = m.weight.dequantize().cpu().numpy().reshape(384, 512).astype(np.float64)
+    xf = x.float().numpy().reshape(-1, 512).astype(np.float64)
+    b = lin.bias.detach().numpy().astype(np.float64)
+    ref = (xf @ w_dq.T + b).reshape(2, 96, 384)
+    mag = (np.abs(xf) @ np.abs(w_dq).T + np.abs(b)).reshape(2, 96, 384)
+    assert np.all(np.abs(out - ref) <= LIN_TOL * mag)
+
+
+@pytest.mark.gpu
+def test_fused_int8_linear_mixed_operands():
+    """Operands the integer GEMM does not take (int8 x against an int4 weight)
+    run as dequant(x) against the packed weight on the K-major kernel."""
+    g = torch.Generator().manual_seed(78)
+    x = torch.randn(9, 256, generator=g)
+    w = torch.randn(64, 256, generator=g) * 0.02
+    xq = mxb.mx_tensor.quantize(x.cuda(), mxb.get_mx_dtype("int8d"), 128)
+    wq = mxb.mx_tensor.quantize(w.cuda(), mxb.get_mx_dtype("int4d"), 128)
+    out = mxb.fused_int8_linear(xq, wq).cpu().numpy().astype(np.float64)
+    x_dq = xq.dequantize().cpu().numpy().astype(np.float64)
+    w_dq = wq.dequantize().cpu().numpy().reshape(64, 256).astype(np.float64)
+    ref, mag = x_dq @ w_dq.T, np.abs(x_dq) @ np.abs(w_dq).T
+    assert np.all(np.abs(out - ref) <= LIN_TOL * mag)

@@ -50,3 +50,33 @@ def test_fused_gather_two_ranks():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert "OK" in r.stdout
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_h_linear_and_quantize_two_ranks():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           os.path.join(HERE, "dist_linear_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert "OK" in r.stdout
+
+
+@pytest.mark.parametrize("N", [1024, 8192])
+def test_kron_split_single_rank(N):
+    """World 1 with the split (G = 1): the local transform of all N columns
+    (unit signs) and the sign stage do the module's full-row unrotation's
+    arithmetic in the same order, so the results are identical."""
+    dt = mxb.get_mx_dtype("int4dh")
+    g = torch.Generator().manual_seed(N)
+    lin = torch.nn.Linear(512, N, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(N, 512, generator=g) * 0.02)
+    ml = mxb.mx_linear.from_linear(lin.cuda(), dt, 128)
+    x = torch.randn(48, 512, generator=g).bfloat16().cuda()
+    sw = P.ShardedLinearWeight.from_module(ml, 1, 0)
+    assert sw.kron_split
+    y = P.sharded_linear(x, sw)
+    ref = ml(x)
+    assert torch.equal(y, ref)

@@ -90,7 +90,11 @@ def test_config4_linear_full_size(int4dh_8192, mode):
     n = 8192
     cols = np.sort(np.random.default_rng(44).choice(n, 62, replace=False))
     cols = np.concatenate([[0], cols, [n - 1]])
-    D = ml._mx_weight.dequantize().double()  # rotated-domain dequantized W^T [K, N]
+    q = ml._mx_weight
+    # rotated-domain dequantized W^T [K, N]: the base dtype's dequantize (the
+    # mx_tensor's own dequantize would also unrotate)
+    D = ops.dequantize(q._mx_packed, q._mx_scales, dt.base, q._mx_n, q._mx_block,
+                       q._mx_orig_shape).double()
     x64 = x.double()
     signs = mxb.sign_vector(n, dt.hadamard_seed).double().cuda()
     Hc = torch.from_numpy(_hadamard_cols(n, cols)).cuda()

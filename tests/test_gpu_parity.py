@@ -352,3 +352,30 @@ def test_qgemm_kmajor_rejects_straddling_blocks():
     qbt = mxb.mx_tensor.quantize(torch.randn(16, 200).cuda(), mxb.int8d, 128)
     with pytest.raises(L.MxbError):
         mxb.mx_matmul_kmajor(qa, qbt)
+
+
+@pytest.mark.parametrize("M", [1, 2])
+@pytest.mark.parametrize("dt", ["int4d", "int8d"])
+@pytest.mark.parametrize("K,N,block,x_dt", [
+    (4096, 11008, 128, torch.bfloat16),   # configs[2]: 43 groups of 256 columns
+    (1000, 640, 64, torch.float32),       # K not a multiple of 32, last group half wide
+    (333, 512, 256, torch.bfloat16),      # group wider than N
+    (96, 256, 32, torch.float32),         # fewer units than SMs
+    (8192, 3072, 1024, torch.bfloat16),   # one scale per group row
+])
+def test_streamed_gemv(M, dt, K, N, block, x_dt):
+    """The streamed TMA GEMV (M <= 2, int4 / int8): runs that cross group
+    boundaries, ragged K, half-width last groups, block sizes below and
+    above the 256-column group, fp32 and bf16 x; and a second call that
+    reuses the workspace."""
+    d = get_mx_dtype(dt)
+    g = torch.Generator().manual_seed(K + N + M)
+    w = torch.randn(K, N, generator=g) * 0.02
+    q = mxb.mx_tensor.quantize(w.cuda(), d, block)
+    wdq = O.dequantize(q._mx_packed.cpu().numpy(), q._mx_scales.cpu().numpy(), d.bits, d.kind,
+                       (K, N), block)
+    for call in range(2):
+        x = torch.randn(M, K, generator=g).to(x_dt)
+        y = ops.linear_wonly(x.cuda(), q._mx_packed, q._mx_scales, K, N, d, block)
+        assert L.load().mxb_device_error(1) == 0
+        _linear_check(y.cpu().numpy(), x.float().numpy(), wdq)
