@@ -182,48 +182,43 @@ def make_inputs():
     return a, b
 
 
-# ── reference arm: the CPU oracle port on the host cores ─────────────────────
-def cpu_baseline_sample(rows=256, reps=1):
-    """Reference path on the host: quantize A-rows + B, packed int GEMM, requant
-    (oracle port of mxtorch.py:1426-1463, 1299-1385) on a row sample of A."""
-    from oracle import mx_oracle as O
+# ── reference arm: the reference's CPU path, as the torch-CPU port ──────────
+def cpu_full_job():
+    """The whole configs[1] job on the host cores: int8d quantize of A and B,
+    the packed int matmul and the int16d requantize (oracle/port_torch.py: the
+    reference's CPU algorithm on torch's multithreaded CPU kernels, bit-exact
+    to the reference's output; in the survey container it took 0.82x the
+    reference's own time for this job).  Returns (TOPS, seconds)."""
+    from oracle import port_torch as PT
     a, b = make_inputs()
-    a = a[:rows].numpy()
-    b = b.numpy()
-    ts = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        pa, sa, _ = O.quantize(a, 8, "int", BLOCK)
-        pb, sb, _ = O.quantize(b, 8, "int", BLOCK)
-        ca = O.unpack(pa, 8, a.size)
-        cb = O.unpack(pb, 8, b.size)
-        O.qscale_matmul(ca, sa, cb, sb, rows, K, N, BLOCK, 16)
-        ts.append(time.perf_counter() - t0)
-    t = min(ts)
-    return 2.0 * rows * N * K / t / 1e12, t
+    t0 = time.perf_counter()
+    PT.int8_job(a, b, BLOCK)
+    t = time.perf_counter() - t0
+    return 2.0 * M * N * K / t / 1e12, t
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    rows = 128
     vals = []
     for i in range(args.warmup + args.steps):
-        v, t = cpu_baseline_sample(rows)
+        v, t = cpu_full_job()
         if i >= args.warmup:
             vals.append(v)
     v = statistics.median(vals)
-    cores = os.cpu_count()
+    cores = torch.get_num_threads()
     line = {
         "metric": "int8d x int8d packed GEMM throughput (4096^3, block 128)",
         "value": v, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "strong", "dtype": "int8", "data": "synthetic",
         "config": {"workload": "int8d x int8d GEMM M=N=K=4096 block 128 (configs[1])",
-                   "sample": f"{rows} rows of A x full B per step"},
+                   "sample": "the whole job per step"},
         "cpu_baseline": {"value": v, "unit": "TOPS", "cores": cores, "kind": "port",
-                         "sample": f"quantize {rows}x4096 A + 4096x4096 B, GEMM, requant"},
+                         "sample": "whole configs[1] job per step: quantize A and B, matmul, "
+                                   "requantize (torch-CPU port, 0.82x the reference's time "
+                                   "in calibration)"},
         "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "vs_baseline": None,
     }
@@ -248,6 +243,10 @@ def run_ours(args, world, rank, local):
 
     if args.only in ("gemv1", "gemv16", "wo2048", "quant", "dequant"):
         print(json.dumps(run_extras(args, dev, flush, torch.cuda.current_stream(dev), hbm, bf16)))
+        return
+    if args.only == "sweep":  # the full configs[4] sweep (a few minutes), one JSON line
+        print(json.dumps({"sweep": run_sweep(dev, flush, torch.cuda.current_stream(dev), hbm,
+                                             max(3, min(args.steps, 10)))}))
         return
 
     a_h, b_h = make_inputs()
@@ -281,15 +280,27 @@ def run_ours(args, world, rank, local):
             return sharded_qgemm_fused(qa, w, peers)
         return sharded_qgemm(qa, w)
 
-    # GEMM kernel alone (fp32 C, no requantization) for the roofline
-    c32 = torch.empty(M, nl, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    # The GEMM kernel alone, for the roofline: at N = 1 the plain matmul
+    # (int16d requantization fused); at N > 1 the kernel the step runs, its
+    # epilogue storing into every rank's output, without the ordering barrier.
     wsb = lib.mxb_qgemm_workspace_size(M, K, nl, 8, BLOCK)
     ws = L.workspace(wsb, dev)
     cp = torch.empty(lib.mxb_packed_bytes(M * nl, 16, BLOCK) // 4, dtype=torch.int32, device=dev)
     cs = torch.empty(M * nl // BLOCK, dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
 
     def gemm_only():
+        if fused:
+            import ctypes as C
+            out = peers.next()
+            rc = lib.mxb_qgemm_sharded(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales),
+                                       qa._mx_scales.numel(), L.ptr(w.codes), L.ptr(w.scales),
+                                       w.scales.numel(), M, K, nl, 8, BLOCK, N, w.n0, world,
+                                       C.cast(out["ptr_w"], C.c_void_p),
+                                       C.cast(out["ptr_s"], C.c_void_p), L.ptr(ws), wsb,
+                                       torch.cuda.current_stream(dev).cuda_stream)
+            L.check(rc, "mxb_qgemm_sharded")
+            return
         rc = lib.mxb_qgemm(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales), qa._mx_scales.numel(),
                            L.ptr(w.codes), L.ptr(w.scales), w.scales.numel(), M, K, nl, 8,
                            BLOCK, 16, L.ptr(cp), L.ptr(cs), None, L.ptr(ws), wsb,
@@ -312,7 +323,7 @@ def run_ours(args, world, rank, local):
     n0 = lib.mxb_launch_count()
     step()
     launches = (lib.mxb_launch_count() - n0) * args.steps
-    # N > 1: eager steps (the NCCL gather is not graph-captured here)
+    # N > 1: eager steps (the NCCL ordering collective is not graph-captured here)
     step_g = graphed(step, stream) if world == 1 else step
     with Clocks(local) as clk:
         barrier(world)
@@ -323,51 +334,38 @@ def run_ours(args, world, rank, local):
 
     check = check_result(step(), qa, qb, world)
 
-    tg = time_steps(graphed(gemm_only, stream), args.steps, flush, stream)
+    barrier(world)
+    tg = time_steps(graphed(gemm_only, stream) if world == 1 else gemm_only, args.steps, flush,
+                    stream)
+    barrier(world)
     gemm_ms = max_over_ranks(sum(tg) / len(tg), world)
     int8_peak = 2.0 * bf16  # kind::i8 issues twice the bf16 rate on sm_100
     achieved = 2.0 * M * nl * K / (gemm_ms * 1e-3) / 1e12
     traffic = profiled_traffic("qgemm_int8_4096") if world == 1 else None
+    # bytes this rank's epilogue stores into its peers' outputs per launch
+    peer_bytes = (world - 1) * (M * nl * 2 + M * nl // BLOCK * 4) if fused else 0
 
-    # e2e: host fp32 operands -> public API -> host packed result
-    a_pin = a_h.pin_memory()
-    b_pin = b_h.pin_memory()
-
-    # B's upload runs on a side stream while A is uploaded and quantized; the
-    # packed result comes back into pinned host buffers.
-    side = torch.cuda.Stream(dev)
-    out_words = torch.empty(M * nl // 2 * world, dtype=torch.int32, pin_memory=True)
-    out_scales = torch.empty(M * N // BLOCK, dtype=torch.float32, pin_memory=True)
-    xa = torch.empty(M, K, dtype=torch.float32, device=dev)
-    xb = torch.empty(K, N, dtype=torch.float32, device=dev)
-
-    def e2e_step():
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            xb.copy_(b_pin, non_blocking=True)
-        xa.copy_(a_pin, non_blocking=True)
-        ea = mxb.mx_tensor.quantize(xa, mxb.int8d, BLOCK)
-        torch.cuda.current_stream(dev).wait_stream(side)
-        eb = mxb.mx_tensor.quantize(xb, mxb.int8d, BLOCK)
-        ew = ShardedQGemmWeight(eb, world, rank)
-        ec = sharded_qgemm_fused(ea, ew, peers) if fused else sharded_qgemm(ea, ew)
-        out_words.copy_(ec._mx_packed, non_blocking=True)
-        out_scales.copy_(ec._mx_scales, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
-        return out_words, out_scales
-
+    # e2e: host fp32 operands -> public API -> host packed result.  Each rank
+    # uploads its rows of A and its columns of B (whole 128-column blocks),
+    # quantizes them (row-sharded quantize, no communication), all-gathers
+    # A's codes and every rank's B block scales (the reference's B-scale view
+    # pairs a column with other rows' blocks), runs the sharded matmul and
+    # reads back its rows of the replicated result.
+    e2e_step, h2d, d2h = make_e2e_step(a_h, b_h, w, peers, fused, world, rank, dev)
     for _ in range(2):
         e2e_step()
     barrier(world)
     te = []
     for _ in range(args.steps):  # host wall clock: the caller's view of one call
-        torch.cuda.synchronize()
+        barrier(world)
         t0 = time.perf_counter()
-        pk, sc = e2e_step()
+        e2e_step()
         te.append((time.perf_counter() - t0) * 1e3)
     e2e_ms = max_over_ranks(sum(te) / len(te), world)
-    h2d = a_h.numel() * 4 + b_h.numel() * 4
-    d2h = pk.numel() * pk.element_size() + sc.numel() * 4
+
+    sharded3 = None
+    if not args.no_extra:
+        sharded3 = run_config3_sharded(args, world, rank, dev, flush, stream, bf16)
 
     extra = {}
     if world == 1 and not args.no_extra:
@@ -377,10 +375,12 @@ def run_ours(args, world, rank, local):
         cpu = None
         if world == 1:
             torch.set_num_threads(os.cpu_count() or 1)
-            v_cpu, t_cpu = cpu_baseline_sample(128)
-            cpu = {"value": v_cpu, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port",
-                   "sample": "quantize 128x4096 A rows + 4096x4096 B, int GEMM, requant "
-                             f"({t_cpu:.2f} s)"}
+            cpu_full_job()  # warm-up
+            v_cpu, t_cpu = cpu_full_job()
+            cpu = {"value": v_cpu, "unit": "TOPS", "cores": torch.get_num_threads(),
+                   "kind": "port",
+                   "sample": f"whole configs[1] job ({t_cpu:.2f} s): quantize A and B, matmul, "
+                             "requantize (torch-CPU port of the reference's CPU path)"}
         line = {
             "metric": "int8d x int8d packed GEMM throughput (4096^3, block 128)",
             "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
@@ -396,18 +396,146 @@ def run_ours(args, world, rank, local):
                        "l2": "flushed (256 MiB write) before every timed step"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak,
                          "unit": "TOPS", "frac": achieved / int8_peak, "traffic": traffic,
-                         "kernel": "qgemm_tc_kernel (int16d requantization fused)",
+                         "kernel": "qgemm_tc_kernel (int16d requantization fused"
+                                   + (", stores into every rank's output)" if fused else ")"),
                          "peak_note": f"2x {peak_src} bf16 burst {bf16} TFLOP/s"},
             "cpu_baseline": cpu,
             "e2e": {"value": 2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                     "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
+            "gemm_ms": gemm_ms,
+            "nvlink": ({"peer_bytes_per_launch": peer_bytes,
+                        "gbs_per_direction": peer_bytes / (gemm_ms * 1e-3) / 1e9,
+                        "link_ref_gbs": 770.0} if fused else None),
+            "config3_sharded": sharded3,
             "check": check,
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
             "extra": extra,
         }
         print(json.dumps(line), flush=True)
+
+
+def make_e2e_step(a_h, b_h, w, peers, fused, world, rank, dev):
+    """One call of the user-facing path from host buffers (see run_ours)."""
+    import qtpytorch_b200 as mxb
+    from qtpytorch_b200 import ops
+    from qtpytorch_b200.parallel import (ShardedQGemmWeight, row_shard, sharded_qgemm,
+                                         sharded_qgemm_fused)
+    r0, r1 = [b * BLOCK // K for b in row_shard(M * K // BLOCK, world, rank)]  # rows of A
+    n0, n1 = w.n0, w.n1
+    nl = n1 - n0
+    a_pin = a_h[r0:r1].contiguous().pin_memory()
+    b_pin = b_h[:, n0:n1].contiguous().pin_memory()  # this rank's columns, prepared once
+    xa = torch.empty(r1 - r0, K, dtype=torch.float32, device=dev)
+    xb = torch.empty(K, nl, dtype=torch.float32, device=dev)
+    side = torch.cuda.Stream(dev)
+    rows_out = (r1 - r0)
+    out_words = torch.empty(rows_out * N // 2, dtype=torch.int32, pin_memory=True)
+    out_scales = torch.empty(rows_out * N // BLOCK, dtype=torch.float32, pin_memory=True)
+    kbn = K // BLOCK
+    shim = ShardedQGemmWeight.__new__(ShardedQGemmWeight)
+    shim.K, shim.N, shim.world, shim.rank, shim.block = K, N, world, rank, BLOCK
+    shim.dtype, shim.shards, shim.n0, shim.n1 = mxb.int8d, w.shards, n0, n1
+
+    def gather(t):
+        if world == 1:
+            return t.unsqueeze(0)
+        import torch.distributed as dist
+        out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous())
+        return out
+
+    def e2e_step():
+        cur = torch.cuda.current_stream(dev)
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            xb.copy_(b_pin, non_blocking=True)
+        xa.copy_(a_pin, non_blocking=True)
+        pa, sa, _ = ops.quantize(xa, mxb.int8d, BLOCK)
+        cur.wait_stream(side)
+        pb, sb, _ = ops.quantize(xb, mxb.int8d, BLOCK)  # blocks = B's blocks of these columns
+        ga, gs = gather(pa), gather(sa)
+        qa = mxb.mx_tensor(ga.reshape(-1), gs.reshape(-1), mxb.int8d, (M, K), M * K, BLOCK)
+        # B's scales of all blocks [K, N/128], rows of N/128 in rank order, then
+        # this shard's slice of the [K/128, N] view
+        sball = gather(sb.view(K, nl // BLOCK)).permute(1, 0, 2).reshape(-1)
+        shim.codes = pb.view(K, nl)
+        shim.scales = sball.view(kbn, N)[:, n0:n1].contiguous()
+        c = sharded_qgemm_fused(qa, shim, peers) if fused else sharded_qgemm(qa, shim)
+        out_words.copy_(c._mx_packed.view(M, N // 2)[r0:r1].reshape(-1), non_blocking=True)
+        out_scales.copy_(c._mx_scales.view(M, N // BLOCK)[r0:r1].reshape(-1), non_blocking=True)
+        cur.synchronize()
+        return out_words, out_scales
+
+    h2d = a_pin.numel() * 4 + b_pin.numel() * 4
+    d2h = out_words.numel() * 4 + out_scales.numel() * 4
+    return e2e_step, h2d, d2h
+
+
+def run_config3_sharded(args, world, rank, dev, flush, stream, bf16):
+    """the int4dh weight-only linear, W 8192 x 8192 ~ N(0, 0.02)
+    with 8 outlier input channels x25, x bf16 [4096, 8192] replicated, W^T
+    column-sharded over the ranks.  Times the rank's GEMM alone and the whole
+    step (GEMM, per-shard transform, all-gather, cross-shard stage), max over
+    ranks, and checks 16 sampled rows against the single-GPU module."""
+    import math
+    import qtpytorch_b200 as mxb
+    from qtpytorch_b200 import _lib as L
+    from qtpytorch_b200 import ops
+    from qtpytorch_b200 import parallel as P
+    g3 = torch.Generator().manual_seed(3)
+    W3 = torch.randn(8192, 8192, generator=g3) * 0.02
+    W3[:, torch.randperm(8192, generator=g3)[:8]] *= 25.0
+    lin3 = torch.nn.Linear(8192, 8192, bias=False)
+    with torch.no_grad():
+        lin3.weight.copy_(W3)
+    dt = mxb.get_mx_dtype("int4dh")
+    ml3 = mxb.mx_linear.from_linear(lin3.to(dev), dt, 128)
+    del W3, lin3
+    x3 = torch.randn(4096, 8192, generator=torch.Generator().manual_seed(4)).bfloat16().to(dev)
+    sw = P.ShardedLinearWeight.from_module(ml3, world, rank)
+    nl = sw.n1 - sw.n0
+
+    def gemm():
+        ops.linear_wonly(x3, sw.codes, sw.scales, 8192, nl, dt, 128)
+
+    def step():
+        return P.sharded_linear(x3, sw)
+
+    for _ in range(3):
+        gemm()
+        step()
+    barrier(world)
+    steps = max(3, min(args.steps, 10))
+    tg = time_steps(graphed(gemm, stream), steps, flush, stream)
+    barrier(world)
+    ts = time_steps(graphed(step, stream) if world == 1 else step, steps, flush, stream)
+    barrier(world)
+    gemm_ms = max_over_ranks(statistics.median(tg), world)
+    step_ms = max_over_ranks(statistics.median(ts), world)
+    y = step()
+    rows = torch.tensor([0, 1, 777, 1500, 2047, 2048, 3001, 4095, 5, 99, 1234, 2500, 3333, 3900,
+                         4000, 4094], device=dev)
+    ref = ml3(x3[rows])
+    q = ml3._mx_weight
+    D = ops.dequantize(q._mx_packed, q._mx_scales, dt.base, q._mx_n, 128, (8192, 8192))
+    bound = (x3[rows].float().abs() @ D.abs()).sum(dim=1, keepdim=True) / math.sqrt(8192)
+    ok = bool(torch.all((y[rows] - ref).abs() <= 2e-5 * bound)) and L.load().mxb_device_error(1) == 0
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    flops = 2.0 * 4096 * 8192 * 8192
+    return {"workload": "int4dh W 8192x8192 (x25 outliers), x bf16 4096x8192, N-sharded "
+                        f"x{world} (configs[3])",
+            "gemm_ms": gemm_ms, "gemm_tflops": flops / world / gemm_ms / 1e9,
+            "gemm_tflops_all_ranks": flops / gemm_ms / 1e9,
+            "step_ms": step_ms, "tflops": flops / step_ms / 1e9,
+            "tensor_frac_bf16": flops / world / gemm_ms / 1e9 / bf16,
+            "unrotation": ("kronecker split" if sw.kron_split and world > 1 else
+                           "full rows" + (" after the gather" if world > 1 else "")),
+            "check": "ok" if int(flag.item()) == 1 else "mismatch"}
 
 
 def check_result(c, qa, qb, world):
@@ -521,28 +649,78 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
                 del p_, s_
         del x
     out["quant_dequant_sweep_2^26"] = sweep
-    # configs[3] on one rank: int4dh weight-only linear, W 8192 x 8192 ~ N(0, 0.02)
-    # with 8 outlier input channels x25, x bf16 [4096, 8192]; the sharded
-    # linear at world 1 (GEMM + the 8192-point unrotation of y)
-    from qtpytorch_b200 import parallel as P
-    g3 = torch.Generator().manual_seed(3)
-    W3 = torch.randn(8192, 8192, generator=g3) * 0.02
-    W3[:, torch.randperm(8192, generator=g3)[:8]] *= 25.0
-    lin3 = torch.nn.Linear(8192, 8192, bias=False)
-    with torch.no_grad():
-        lin3.weight.copy_(W3)
-    ml3 = mxb.mx_linear.from_linear(lin3.to(dev), mxb.get_mx_dtype("int4dh"), 128)
-    del W3, lin3
-    x3 = torch.randn(4096, 8192, generator=torch.Generator().manual_seed(4)).bfloat16().to(dev)
-    sw3 = P.ShardedLinearWeight.from_module(ml3, 1, 0)
-    for _ in range(2):
-        P.sharded_linear(x3, sw3)
-    fn = graphed(lambda: P.sharded_linear(x3, sw3), stream)
-    t = statistics.median(time_steps(fn, steps, flush, stream))
-    flops = 2.0 * 4096 * 8192 * 8192
-    out["wonly_int4dh_8192_M4096_g1"] = {"ms": t, "tflops": flops / t / 1e9,
-                                         "tensor_frac_bf16": flops / t / 1e9 / bf16}
+    out.update(run_h_kernels(dev, flush, stream, hbm, steps))
     return out
+
+
+def run_h_kernels(dev, flush, stream, hbm, steps):
+    """The Hadamard-variant kernels at configs[3] sizes: int4dh quantize and
+    dequantize of W^T 8192 x 8192 (fused 8192-point row WHT) and the row
+    unrotation of y 4096 x 8192; GB/s of algorithmic bytes."""
+    import qtpytorch_b200 as mxb
+    from qtpytorch_b200 import ops
+    out = {}
+    dt = mxb.get_mx_dtype("int4dh")
+    w = torch.randn(8192, 8192, device=dev) * 0.02
+    n = w.numel()
+    p_, s_, _ = ops.quantize(w, dt, 128)
+    fq = graphed(lambda: ops.quantize(w, dt, 128), stream)
+    tq = statistics.median(time_steps(fq, steps, flush, stream))
+    fd = graphed(lambda: ops.dequantize(p_, s_, dt, n, 128, (8192, 8192)), stream)
+    td = statistics.median(time_steps(fd, steps, flush, stream))
+    qb = n * 4 + n / 2 + n / 128 * 4
+    out["quantize_int4dh_8192x8192"] = {"ms": tq, "gbs": qb / tq / 1e6,
+                                         "hbm_frac": qb / tq / 1e6 / hbm}
+    out["dequantize_int4dh_8192x8192"] = {"ms": td, "gbs": qb / td / 1e6,
+                                           "hbm_frac": qb / td / 1e6 / hbm}
+    y = torch.randn(4096, 8192, device=dev)
+    fr = graphed(lambda: ops.hadamard_rows(y, dt.hadamard_seed, True), stream)
+    tr = statistics.median(time_steps(fr, steps, flush, stream))
+    rb = y.numel() * 8
+    out["hadamard_rows_4096x8192"] = {"ms": tr, "gbs": rb / tr / 1e6, "hbm_frac": rb / tr / 1e6 / hbm}
+    return out
+
+
+def run_sweep(dev, flush, stream, hbm, steps):
+    """configs[4] in full: fp32 / bf16 N(0,1) of 2^20 .. 2^30 elements (x4)
+    and a Student-t (nu = 3) tail at 2^26, quantized to int2d / int1d /
+    float4d at blocks 32 and 128, then dequantized; GB/s of algorithmic
+    bytes (quantize: input + codes + scales; dequantize: codes + scales +
+    fp32 output).  Sizes under the L2 capacity are flushed between steps."""
+    import qtpytorch_b200 as mxb
+    from qtpytorch_b200 import ops
+    res = {}
+    cases = [(1 << e, "normal") for e in range(20, 31, 2)] + [(1 << 26, "student_t")]
+    for n, dist_ in cases:
+        torch.cuda.manual_seed(5)
+        if dist_ == "normal":
+            base = torch.randn(n, device=dev)
+        else:
+            base = torch.distributions.StudentT(torch.tensor(3.0, device=dev)).sample((n,))
+        for in_dt in (torch.float32, torch.bfloat16):
+            x = base.to(in_dt)
+            ib = 4 if in_dt == torch.float32 else 2
+            for dt in ("int2d", "int1d", "float4d"):
+                d = mxb.get_mx_dtype(dt)
+                for blk in (32, 128):
+                    p_, s_, _ = ops.quantize(x, d, blk)
+                    fq = graphed(lambda: ops.quantize(x, d, blk), stream)
+                    tq = statistics.median(time_steps(fq, steps, flush, stream))
+                    fd = graphed(lambda: ops.dequantize(p_, s_, d, n, blk), stream)
+                    td = statistics.median(time_steps(fd, steps, flush, stream))
+                    qb = n * ib + n * d.bits / 8 + n / blk * 4
+                    db = n * d.bits / 8 + n / blk * 4 + n * 4
+                    key = (f"2^{n.bit_length() - 1}_{dist_}_{'fp32' if ib == 4 else 'bf16'}_"
+                           f"{dt}_b{blk}")
+                    res[key] = {"q_gbs": round(qb / tq / 1e6, 1),
+                                "q_frac": round(qb / tq / 1e6 / hbm, 3),
+                                "dq_gbs": round(db / td / 1e6, 1),
+                                "dq_frac": round(db / td / 1e6 / hbm, 3)}
+                    del p_, s_
+            del x
+        del base
+        torch.cuda.empty_cache()
+    return res
 
 
 def main():
@@ -554,7 +732,7 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="N > 1: output gather fused into the GEMM kernel, or NCCL all-gather")
-    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant", "dequant"],
+    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant", "dequant", "sweep"],
                     help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -623,15 +623,21 @@ int tc_wonly_dec(const void* x, int64_t M, int64_t K, const void* w, const float
 }
 
 // ── streamed GEMV, M <= 2 (gemv_tma.cuh) ─────────────────────────────────────
+gv::Geometry tma_gemv_geometry(int64_t M, int64_t K, int64_t N, int bits, int block);
+
 bool tma_gemv_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
                        int64_t N, int bits, int kind, int block, const float* y) {
   if (kind != MXB_KIND_INT || (bits != 4 && bits != 8)) return false;
   if (x_dtype != MXB_F32 && x_dtype != MXB_BF16) return false;
   if (M < 1 || M > 2 || K < 1 || N < 1) return false;
+  // unit indices in 32 bits, and R * C below 2^32 for the reduction's
+  // run-start arithmetic
   if (cdiv(N, gv::GC) * cdiv(K, gv::BR) >= ((int64_t)1 << 31)) return false;
   const int cpt = 64 / bits;  // columns of one thread's 8 code bytes
   if (N % 128 || block % cpt || N % block || gv::GC % block) return false;
   if (((uintptr_t)w & 15) || ((uintptr_t)y & 3)) return false;
+  const gv::Geometry geo = tma_gemv_geometry(M, K, N, bits, block);
+  if (geo.R * geo.C >= ((int64_t)1 << 32)) return false;
   return true;
 }
 
@@ -737,6 +743,13 @@ int tma_gemv(const void* x, int x_dtype, int64_t M, int64_t K, const void* w, co
 }
 
 }  // namespace mxb
+
+#ifdef MXB_GEMV_TRACE
+extern "C" int mxb_debug_gemv_trace(uint64_t* host, int n) {
+  return cudaMemcpyFromSymbol(host, mxb::gv::g_gemv_trace, n * sizeof(uint64_t)) == cudaSuccess
+             ? 0 : -1;
+}
+#endif
 
 extern "C" int mxb_device_error(int clear) {
   int v = 0;

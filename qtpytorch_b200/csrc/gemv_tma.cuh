@@ -32,6 +32,12 @@
 namespace mxb {
 namespace gv {
 
+#ifdef MXB_GEMV_TRACE
+// Timeline probe (never defined in the library build): %globaltimer at phase
+// boundaries of each CTA.
+__device__ uint64_t g_gemv_trace[8192];
+#endif
+
 constexpr int GC = 1024;            // columns per group
 constexpr int BR = 32;              // K rows per unit (one TMA box)
 constexpr int kComputeWarps = 16;
@@ -125,6 +131,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + stages;
 
   const int C = gridDim.x, c = blockIdx.x;
+#ifdef MXB_GEMV_TRACE
+  if (threadIdx.x == 0) g_gemv_trace[c * 4 + 0] = globaltimer_ns();
+#endif
   // unit indices fit 32 bits (the host checks R < 2^31): 32-bit div / mod below
   const int u0 = (int)run_start(c, R, C), u1 = (int)run_start(c + 1, R, C);
   const int nu = u1 - u0;
@@ -166,20 +175,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ── x and scales of the run's rows (plain loads, in flight with the boxes) ──
   const int nsb = N / block;
-  for (int i = threadIdx.x; i < nu * BR; i += kComputeThreads) {
-    const int u = u0 + i / BR;
-    const int k = (u % KB) * BR + i % BR;
+  // scales: asynchronous 4-byte copies, all in flight at once (zero-filled
+  // past K or past the last scale column); x: plain loads
+  const int spr_log = 31 - __clz(spr);  // spr = GC / block, a power of two
+  for (int e = threadIdx.x; e < (nu * BR) << spr_log; e += kComputeThreads) {
+    const int li = e >> spr_log, j = e & (spr - 1);
+    const int u = u0 + li / BR;  // BR is a power of two
+    const int g = u / KB, k = (u - g * KB) * BR + li % BR;
+    const int sc = g * spr + j;
+    const bool in = k < K && sc < nsb;
+    const float* src = in ? ws + (int64_t)k * nsb + sc : ws;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(ss + e)),
+                 "l"(src), "r"(in ? 4 : 0)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int li = threadIdx.x; li < nu * BR; li += kComputeThreads) {
+    const int u = u0 + li / BR;
+    const int k = (u % KB) * BR + li % BR;
 #pragma unroll
     for (int m = 0; m < MT; ++m)
-      xs[i * MT + m] = (k < K && m < M) ? load_as_f32(x, (int64_t)m * K + k) : 0.0f;
+      xs[li * MT + m] = (k < K && m < M) ? load_as_f32(x, (int64_t)m * K + k) : 0.0f;
   }
-  for (int i = threadIdx.x; i < nu * BR * spr; i += kComputeThreads) {
-    const int row = i / spr, j = i % spr;
-    const int u = u0 + row / BR;
-    const int g = u / KB, k = (u % KB) * BR + row % BR;
-    const int sc = g * spr + j;
-    ss[i] = (k < K && sc < nsb) ? __ldg(ws + (int64_t)k * nsb + sc) : 0.0f;
-  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+#ifdef MXB_GEMV_TRACE
+  if (threadIdx.x == 0) g_gemv_trace[c * 4 + 1] = globaltimer_ns();
+#endif
   compute_bar();  // named barrier over the compute warps only (the producer has left)
 
   const int t = threadIdx.x;
@@ -269,7 +290,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
+#ifdef MXB_GEMV_TRACE
+  if (threadIdx.x == 0) g_gemv_trace[c * 4 + 2] = globaltimer_ns();
+#endif
   if (nu > 0) flush();
+#ifdef MXB_GEMV_TRACE
+  if (threadIdx.x == 0) g_gemv_trace[c * 4 + 3] = globaltimer_ns();
+#endif
 }
 
 // y[m, n] = sum over the CTAs whose runs cover n's group, in CTA order, of
@@ -283,19 +310,29 @@ __global__ void __launch_bounds__(256) gemv_tma_reduce(const float* __restrict__
                                                        float* __restrict__ y) {
   __shared__ int slots[kMaxContrib];
   __shared__ int nslots;
+#ifdef MXB_GEMV_TRACE
+  const int tb = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  if (threadIdx.x == 0) g_gemv_trace[4096 + tb * 3 + 0] = globaltimer_ns();
+#endif
   asm volatile("griddepcontrol.wait;" ::: "memory");
+#ifdef MXB_GEMV_TRACE
+  if (threadIdx.x == 0) g_gemv_trace[4096 + tb * 3 + 1] = globaltimer_ns();
+#endif
   const int g = blockIdx.y, m = blockIdx.z;
   const int64_t gs = (int64_t)g * KB, ge = gs + KB;
   if (threadIdx.x < 32) {
+    // run starts in 32-bit arithmetic (the host keeps R * C below 2^32)
+    const uint32_t uR = (uint32_t)R, uC = (uint32_t)C;
+    auto start32 = [&](uint32_t c) -> int64_t { return (int64_t)((c * uR) / uC); };
     // first CTA whose run holds unit gs
-    int64_t cl = gs * C / R;
-    while (cl > 0 && run_start(cl, R, C) > gs) --cl;
-    while (cl + 1 < C && run_start(cl + 1, R, C) <= gs) ++cl;
+    int64_t cl = (int64_t)(((uint64_t)gs * uC) / uR);
+    while (cl > 0 && start32((uint32_t)cl) > gs) --cl;
+    while (cl + 1 < C && start32((uint32_t)(cl + 1)) <= gs) ++cl;
     int n = 0;
     for (int64_t base = cl; base < C; base += 32) {
       const int64_t cc = base + threadIdx.x;
-      const int64_t a = cc < C ? run_start(cc, R, C) : ge;
-      const int64_t b = cc < C ? run_start(cc + 1, R, C) : ge;
+      const int64_t a = cc < C ? start32((uint32_t)cc) : ge;
+      const int64_t b = cc < C ? start32((uint32_t)(cc + 1)) : ge;
       const bool in = cc < C && a < ge && b > a && b > gs;
       const unsigned mask = __ballot_sync(0xffffffffu, in);
       if (in) {
@@ -315,16 +352,19 @@ __global__ void __launch_bounds__(256) gemv_tma_reduce(const float* __restrict__
   const float* base = part + (size_t)m * GC + col;
   float sum = 0.0f;
   const int ns = nslots;
-  for (int i0 = 0; i0 < ns; i0 += 8) {
-    float v[8];
+  for (int i0 = 0; i0 < ns; i0 += 16) {
+    float v[16];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 16; ++j)
       v[j] = i0 + j < ns ? __ldcg(base + (size_t)slots[i0 + j] * MT * GC) : 0.0f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 16; ++j)
       if (i0 + j < ns) sum = __fadd_rn(sum, v[j]);
   }
   y[(int64_t)m * N + n] = sum;
+#ifdef MXB_GEMV_TRACE
+  if (threadIdx.x == 0) g_gemv_trace[4096 + tb * 3 + 2] = globaltimer_ns();
+#endif
 }
 
 }  // namespace gv

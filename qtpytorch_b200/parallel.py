@@ -260,7 +260,7 @@ def sharded_linear(x: torch.Tensor, w: ShardedLinearWeight, group=None, mode: st
     md = L.MODE_FAST if mode == "fast" else L.MODE_PARITY
     y = ops.linear_wonly(xm, w.codes, w.scales, K, w.n1 - w.n0, w.dtype, w.block, md)
     h = w.dtype.is_hadamard
-    if h and w.kron_split:
+    if h and w.kron_split and w.world > 1:
         # H_N = H_G (x) H_L: each rank transforms its own L columns, the one
         # all-gather moves those, and one kernel runs the G-point stage, the
         # signs and the reorder to row-major

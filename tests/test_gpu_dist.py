@@ -65,9 +65,10 @@ def test_sharded_h_linear_and_quantize_two_ranks():
 
 @pytest.mark.parametrize("N", [1024, 8192])
 def test_kron_split_single_rank(N):
-    """World 1 with the split (G = 1): the local transform of all N columns
-    (unit signs) and the sign stage do the module's full-row unrotation's
-    arithmetic in the same order, so the results are identical."""
+    """G = 1 of the split: the local transform of all N columns (unit signs)
+    and the sign stage (mxb_hadamard_cross) do the module's full-row
+    unrotation's arithmetic in the same order, so the results are identical;
+    sharded_linear itself skips the split at world 1."""
     dt = mxb.get_mx_dtype("int4dh")
     g = torch.Generator().manual_seed(N)
     lin = torch.nn.Linear(512, N, bias=False)
@@ -77,6 +78,10 @@ def test_kron_split_single_rank(N):
     x = torch.randn(48, 512, generator=g).bfloat16().cuda()
     sw = P.ShardedLinearWeight.from_module(ml, 1, 0)
     assert sw.kron_split
-    y = P.sharded_linear(x, sw)
+    from qtpytorch_b200 import ops
+    y0 = ops.linear_wonly(x, sw.codes, sw.scales, 512, N, dt, 128)
+    t = ops.hadamard_rows(y0, None, inverse=True)
+    y = ops.hadamard_cross(t, 48, N, 1, dt.hadamard_seed)
     ref = ml(x)
     assert torch.equal(y, ref)
+    assert torch.equal(P.sharded_linear(x, sw), ref)

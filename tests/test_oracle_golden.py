@@ -103,3 +103,19 @@ def test_wht_matches_reference(golden):
     g = torch.Generator().manual_seed(11)
     xw = torch.randn(2, 1024, generator=g).numpy()
     assert np.array_equal(O.fwht(xw), golden["wht/y"])
+
+
+@pytest.mark.parametrize("c", [c for c in cases.GEMM_CASES
+                               if c["dtype"] == "int8d" and "dtype_b" not in c],
+                         ids=lambda c: c["key"])
+def test_torch_port_matches_reference(golden, c):
+    """The torch-CPU port that bench.py times as the CPU baseline gives the
+    reference's packed result bit for bit (int8d, all configs[1]-style cases)."""
+    from oracle import port_torch as PT
+    a, b = cases.make_gemm_inputs(c)
+    M, K, N = c["M"], c["K"], c["N"]
+    ca, sa, _ = PT.quantize_int(a, 8, c["block"])
+    cb, sb, _ = PT.quantize_int(b, 8, c["block"])
+    codes, cs = PT.qscale_matmul(ca, sa, cb, sb, M, K, N, c["block"], 16)
+    assert np.array_equal(PT.pack16(codes).numpy(), golden[f"{c['key']}/c_packed"])
+    assert np.array_equal(cs.numpy().view(np.uint32), golden[f"{c['key']}/c_scales"].view(np.uint32))
