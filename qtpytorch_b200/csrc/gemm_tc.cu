@@ -153,11 +153,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int col0 = (ew >> 2) * kEpiCols;  // this warp's column slice
     const int row = q * 32 + lane;
     const int m = m0 + row;
-    // fp32 accumulator as packed pairs (f32x2 ops round each lane like the
-    // scalar op, so results stay bit-identical)
-    uint64_t acc[kEpiCols / 2];
+    // fp32 accumulator, one register per column (the adds are scalar; the
+    // products are packed f32x2 pairs, which round each lane like the scalar
+    // op, so results stay bit-identical)
+    float acc[kEpiCols];
 #pragma unroll
-    for (int c = 0; c < kEpiCols / 2; ++c) acc[c] = 0ull;
+    for (int c = 0; c < kEpiCols; ++c) acc[c] = 0.0f;
     // Scales are fetched one K-block ahead: sa (one per row) into a register,
     // this warp's sb slice one value per lane, staged through a per-warp
     // double buffer in shared memory and read back as broadcasts.
@@ -199,28 +200,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           // products packed; the add stays scalar so it is never fused
           // with the multiply (a fused add would skip one rounding)
           const float2 t = unpack2(fmul2(fmul2(pf, sa2), sv[j]));
-          const float2 a = unpack2(acc[c / 2]);
-          acc[c / 2] = pack2(__fadd_rn(a.x, t.x), __fadd_rn(a.y, t.y));
+          acc[c] = __fadd_rn(acc[c], t.x);
+          acc[c + 1] = __fadd_rn(acc[c + 1], t.y);
         }
       }
     }
     if (C != nullptr) {
       float4* out = reinterpret_cast<float4*>(C + (size_t)m * N + n0 + col0);
 #pragma unroll
-      for (int c4 = 0; c4 < kEpiCols / 4; ++c4) {
-        const float2 lo = unpack2(acc[2 * c4]), hi = unpack2(acc[2 * c4 + 1]);
-        out[c4] = make_float4(lo.x, lo.y, hi.x, hi.y);
-      }
+      for (int c4 = 0; c4 < kEpiCols / 4; ++c4)
+        out[c4] = make_float4(acc[4 * c4], acc[4 * c4 + 1], acc[4 * c4 + 2], acc[4 * c4 + 3]);
     }
     if (qout.count > 0) {
       // Fused int16d requantization (mxtorch.py:1371-1378): the 128 columns
       // of this tile row are one scale block (N % 128 == 0, block 128).
       float a = 0.0f;
 #pragma unroll
-      for (int c = 0; c < kEpiCols / 2; ++c) {
-        const float2 v = unpack2(acc[c]);
-        a = amax_step(amax_step(a, v.x), v.y);
-      }
+      for (int c = 0; c < kEpiCols; ++c) a = amax_step(a, acc[c]);
       bars->slice_amax[ew >> 2][row] = a;
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");  // promotion warps only
 #pragma unroll
@@ -229,9 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t w[kEpiCols / 2];
 #pragma unroll
       for (int c = 0; c < kEpiCols / 2; ++c) {
-        const float2 v = unpack2(acc[c]);
         uint32_t code[2];
-        const float vv[2] = {v.x, v.y};
+        const float vv[2] = {acc[2 * c], acc[2 * c + 1]};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const float qv = nan_min(nan_max(__fdiv_rn(vv[h], cs), -32767.0f), 32767.0f);
@@ -635,7 +630,8 @@ bool tma_gemv_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const v
   if (cdiv(N, gv::GC) * cdiv(K, gv::BR) >= ((int64_t)1 << 31)) return false;
   const int cpt = 64 / bits;  // columns of one thread's 8 code bytes
   if (N % 128 || block % cpt || N % block || gv::GC % block) return false;
-  if (((uintptr_t)w & 15) || ((uintptr_t)y & 3)) return false;
+  // x arrives in 16-byte chunks: rows of whole chunks, 16-byte aligned
+  if (((uintptr_t)w & 15) || ((uintptr_t)y & 3) || ((uintptr_t)x & 15) || K % 8) return false;
   const gv::Geometry geo = tma_gemv_geometry(M, K, N, bits, block);
   if (geo.R * geo.C >= ((int64_t)1 << 32)) return false;
   return true;

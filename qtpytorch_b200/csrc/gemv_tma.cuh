@@ -39,7 +39,7 @@ __device__ uint64_t g_gemv_trace[8192];
 #endif
 
 constexpr int GC = 1024;            // columns per group
-constexpr int BR = 32;              // K rows per unit (one TMA box)
+constexpr int BR = 64;              // K rows per unit (one TMA box)
 constexpr int kComputeWarps = 16;
 constexpr int kComputeThreads = 32 * kComputeWarps;
 constexpr int kThreads = kComputeThreads + 32;  // + producer warp
@@ -84,23 +84,48 @@ __host__ __device__ inline size_t smem_layout(int stages, int umax, int spr, siz
   return o + 128;  // alignment slack of the base
 }
 
-// Bounded wait that backs off with __nanosleep between polls, so warps that
-// run ahead of the arriving boxes leave the issue slots to the warps that
-// have data.  Warp-uniform result.
+// Bounded wait in which only lane 0 of the warp polls, backing off with
+// __nanosleep between polls, so the warps that run ahead of the arriving
+// boxes neither crowd the barrier word the copy engine is updating nor take
+// issue slots from the warps that have data.  Warp-uniform result.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int err_code) {
-  bool ok = mbar_test_wait(bar, parity);
-  if (!__all_sync(0xffffffffu, ok)) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0 && !mbar_test_wait(bar, parity)) {
     const uint64_t t0 = globaltimer_ns();
     ok = false;
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
-      if (mbar_try_wait(bar, parity)) { ok = true; break; }
-      __nanosleep(64);
+      __nanosleep(32);
+      if (mbar_test_wait(bar, parity)) { ok = true; break; }
       if ((i & 15) == 15 && globaltimer_ns() - t0 > kWaitLimitNs) break;
     }
     if (!ok) atomicCAS(&g_mxb_device_error, 0, err_code);
-    ok = __all_sync(0xffffffffu, ok);
   }
-  return ok;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  // the other lanes observe the completed phase themselves (memory ordering
+  // of the box's bytes for this thread)
+  if (ok) ok = mbar_test_wait(bar, parity) || mbar_try_wait(bar, parity);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__device__ __forceinline__ uint2 lds_u32x2(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+template <typename XT>
+__device__ __forceinline__ float lds_as_f32(uint32_t a) {
+  if constexpr (sizeof(XT) == 4) {
+    return lds_f32(a);
+  } else {  // bf16: the upper half of an fp32
+    unsigned short h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+    return __uint_as_float((uint32_t)h << 16);
+  }
 }
 
 __device__ __forceinline__ void compute_bar() {
@@ -146,6 +171,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_barrier_init();
   }
+  // ── x and scales of the run's rows: asynchronous copies, issued before
+  // any weight box so they are not queued behind the 24 MB stream (scales 4
+  // bytes each, x 16-byte chunks; zero-filled past K or the last scale
+  // column).  x is kept in its own type, [MT][nu * BR].
+  const int nsb = N / block;
+  XT* xr = reinterpret_cast<XT*>(xs);
+  if (warp < kComputeWarps) {
+    const int spr_log = 31 - __clz(spr);  // spr = GC / block, a power of two
+    for (int e = threadIdx.x; e < (nu * BR) << spr_log; e += kComputeThreads) {
+      const int li = e >> spr_log, j = e & (spr - 1);
+      const int u = u0 + li / BR;  // BR is a power of two
+      const int g = u / KB, k = (u - g * KB) * BR + li % BR;
+      const int sc = g * spr + j;
+      const bool in = k < K && sc < nsb;
+      const float* src = in ? ws + (int64_t)k * nsb + sc : ws;
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(ss + e)),
+                   "l"(src), "r"(in ? 4 : 0)
+                   : "memory");
+    }
+    constexpr int XC = 16 / sizeof(XT);  // x elements per 16-byte chunk (K % XC == 0)
+    const int nch = nu * (BR / XC);
+    for (int e = threadIdx.x; e < MT * nch; e += kComputeThreads) {
+      const int m = e / nch, cidx = e % nch;
+      const int iu = cidx / (BR / XC), k = ((u0 + iu) % KB) * BR + (cidx % (BR / XC)) * XC;
+      const bool in = k < K && m < M;
+      const XT* src = in ? x + (int64_t)m * K + k : x;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                       smem_u32(xr + (size_t)m * nu * BR + iu * BR + (cidx % (BR / XC)) * XC)),
+                   "l"(src), "r"(in ? 16 : 0)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   __syncthreads();
   // let the partial-sum reduction kernel start launching (it waits for this
   // grid's completion before reading anything)
@@ -165,37 +223,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(ring + (size_t)s * BR * GB, &tmap_w, &full[s], g * (GB / 8), rb * BR);
         issued = i + 1;
       }
+#ifdef MXB_GEMV_TRACE
+      if (c == 0)
+        for (int i = 0; i < issued && i < stages && i < 64; ++i) {
+          mbar_wait(&full[i], 0, kErrTimeoutFull);
+          g_gemv_trace[7000 + i] = globaltimer_ns();
+        }
+#endif
       // No box may still be landing when the CTA exits: wait (bounded) for
       // the last box of every stage (already complete on the normal path).
       for (int i = issued > stages ? issued - stages : 0; i < issued; ++i)
         mbar_wait(&full[i % stages], (i / stages) & 1, kErrTimeoutFull);
     }
     return;
-  }
-
-  // ── x and scales of the run's rows (plain loads, in flight with the boxes) ──
-  const int nsb = N / block;
-  // scales: asynchronous 4-byte copies, all in flight at once (zero-filled
-  // past K or past the last scale column); x: plain loads
-  const int spr_log = 31 - __clz(spr);  // spr = GC / block, a power of two
-  for (int e = threadIdx.x; e < (nu * BR) << spr_log; e += kComputeThreads) {
-    const int li = e >> spr_log, j = e & (spr - 1);
-    const int u = u0 + li / BR;  // BR is a power of two
-    const int g = u / KB, k = (u - g * KB) * BR + li % BR;
-    const int sc = g * spr + j;
-    const bool in = k < K && sc < nsb;
-    const float* src = in ? ws + (int64_t)k * nsb + sc : ws;
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(ss + e)),
-                 "l"(src), "r"(in ? 4 : 0)
-                 : "memory");
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  for (int li = threadIdx.x; li < nu * BR; li += kComputeThreads) {
-    const int u = u0 + li / BR;
-    const int k = (u % KB) * BR + li % BR;
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-      xs[li * MT + m] = (k < K && m < M) ? load_as_f32(x, (int64_t)m * K + k) : 0.0f;
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
 #ifdef MXB_GEMV_TRACE
@@ -207,17 +247,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ch = t % CH, p = t / CH;
   const int col0 = ch * CPT;       // first column of this thread in the group
   const int sj = col0 / block;     // scale slot of this thread's chunk
-  uint64_t acc[MT][CPT / 2];
+  // two accumulator sets, even and odd rows of a unit: twice the
+  // independent FMA chains; added in a fixed order at the flush
+  uint64_t acc[MT][CPT / 2], acc2[MT][CPT / 2];
 #pragma unroll
   for (int m = 0; m < MT; ++m)
 #pragma unroll
-    for (int q = 0; q < CPT / 2; ++q) acc[m][q] = 0ull;
+    for (int q = 0; q < CPT / 2; ++q) acc[m][q] = acc2[m][q] = 0ull;
 
   int cur_g = u0 / KB;
   int seg = 0;
   // Phase sums in a fixed order: red[p] = acc(p) for p < P/2, then
   // red[p - P/2] += acc(p), then the P/2 rows added in order.
   auto flush = [&]() {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int q = 0; q < CPT / 2; ++q) {
+        const float2 a = unpack2(acc[m][q]), b = unpack2(acc2[m][q]);
+        acc[m][q] = pack2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+        acc2[m][q] = 0ull;
+      }
     if (p < P / 2) {
 #pragma unroll
       for (int m = 0; m < MT; ++m)
@@ -254,6 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int q = 0; q < CPT / 2; ++q) acc[m][q] = 0ull;
   };
 
+  const uint32_t ring_a = smem_u32(ring) + p * GB + ch * 8;
+  const uint32_t ss_a = smem_u32(ss) + (uint32_t)(p * spr + sj) * 4u;
+  const uint32_t ss_row = (uint32_t)(P * spr * 4), ss_unit = (uint32_t)(BR * spr * 4);
+  const uint32_t x_a = smem_u32(xr) + (uint32_t)(p * sizeof(XT));
+  const uint32_t x_unit = BR * sizeof(XT), x_m = (uint32_t)(nu * BR * sizeof(XT));
   // After a wait gives up (its code is in the device error word) the warp
   // stops waiting but keeps every barrier of the loop, so no warp is left
   // alone at a named barrier; the outputs are then invalid.
@@ -267,24 +322,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int s = i % stages, round = i / stages;
     if (!failed && !mbar_wait_sleep(&full[s], round & 1, kErrTimeoutFull)) failed = true;
-    const uint8_t* box = ring + (size_t)s * BR * GB;
+#ifdef MXB_GEMV_TRACE
+    if (c == 0 && threadIdx.x == 0 && i < 64) g_gemv_trace[6000 + i] = globaltimer_ns();
+#endif
+    // shared-memory addresses as 32-bit offsets: stage, row and unit steps
+    // are constants or one add
+    const uint32_t box_a = ring_a + (uint32_t)(s * BR * GB);
     uint2 wv[RPT];
 #pragma unroll
-    for (int rr = 0; rr < RPT; ++rr)
-      wv[rr] = *reinterpret_cast<const uint2*>(box + (p + rr * P) * GB + ch * 8);
+    for (int rr = 0; rr < RPT; ++rr) wv[rr] = lds_u32x2(box_a + rr * P * GB);
+    const uint32_t ss_i = ss_a + (uint32_t)i * ss_unit, x_i = x_a + (uint32_t)i * x_unit;
 #pragma unroll
     for (int rr = 0; rr < RPT; ++rr) {
-      const int li = i * BR + p + rr * P;
-      const float sc = ss[li * spr + sj];
+      const float sc = lds_f32(ss_i + rr * ss_row);
       uint64_t code[CPT / 2];
       decode_word2<BITS>(wv[rr].x, code);
       decode_word2<BITS>(wv[rr].y, code + CPT / 4);
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
-        const float xv = __fmul_rn(xs[li * MT + m], sc);
+        const float xv = __fmul_rn(lds_as_f32<XT>(x_i + m * x_m + rr * P * (int)sizeof(XT)), sc);
         const uint64_t x2 = pack2(xv, xv);
+        if (rr & 1) {
 #pragma unroll
-        for (int q = 0; q < CPT / 2; ++q) acc[m][q] = ffma2(x2, code[q], acc[m][q]);
+          for (int q = 0; q < CPT / 2; ++q) acc2[m][q] = ffma2(x2, code[q], acc2[m][q]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < CPT / 2; ++q) acc[m][q] = ffma2(x2, code[q], acc[m][q]);
+        }
       }
     }
     __syncwarp();

@@ -10,6 +10,7 @@
 // true division for float4 and for the matmul requantization, round half to
 // even.  Built without fast-math so every `__f*_rn` is one IEEE rounding.
 #include "mxb_common.cuh"
+#include "wht_regs.cuh"
 
 #include <math.h>
 #include <stdint.h>
@@ -751,8 +752,174 @@ __global__ void __launch_bounds__(256) hrows_kernel(const float* __restrict__ x,
   }
 }
 
+// ── the same three kernels with the row in registers (n = 256 * V) ─────────
+// Bit-identical to the shared-memory versions above (same stage order and
+// rounding, whtr::div_sqrtn equal to the IEEE quotient where selected); two
+// passes through shared memory instead of one per radix pass plus the
+// shuffle stages, and the row leaves in runs of consecutive elements.
+
+template <typename InT, int BITS, int MODE, int V>
+__global__ void __launch_bounds__(256) hquant_fast_kernel(
+    const InT* __restrict__ x, int d, float sqrtn, float rsq, int dmode,
+    const float* __restrict__ signs, int block, bool fuse_quant, uint8_t* __restrict__ packed,
+    float* __restrict__ scales, float* __restrict__ rot_out) {
+  using W = whtr::Row<V>;
+  extern __shared__ __align__(16) float srow[];
+  const int64_t r = blockIdx.x;
+  const InT* xr = x + r * d;
+  const int t = threadIdx.x;
+  float v[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = W::idxA(t, j);
+    v[j] = i < d ? __fmul_rn(load_as_f32(xr, i), __ldg(signs + i)) : 0.0f;
+  }
+  W::transform(v, srow);
+#pragma unroll
+  for (int j = 0; j < V; ++j) v[j] = whtr::div_sqrtn(v[j], sqrtn, rsq, dmode);
+  if (!fuse_quant) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int i = W::idx(t, j);
+      if (i < d) rot_out[r * d + i] = v[j];
+    }
+    return;
+  }
+  const int64_t row_e0 = r * (int64_t)d;
+  constexpr int E = W::kG;  // run length: 8 or 16 consecutive elements
+  if constexpr (W::kPhaseC && (E == 8 || E == 16)) {
+    if (block % E == 0) {
+      // runs of E consecutive elements in consecutive lanes: block / E lanes
+      // form a block, exactly the layout quant8_store takes
+      const int L = block / E;
+#pragma unroll
+      for (int q = 0; q < W::kRuns; ++q) {
+        const int i0 = W::idx(t, q * E);
+        const bool valid = i0 < d;
+        quant8_store<BITS, MODE, E>(*reinterpret_cast<float(*)[E]>(v + q * E), valid, L,
+                                    row_e0 + i0, packed, scales, (row_e0 + i0) / block);
+      }
+      return;
+    }
+  }
+  // other run lengths: through shared memory in natural order
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = W::idx(t, j);
+    if (i < d) srow[i] = v[j];
+  }
+  __syncthreads();
+  // d % block == 0 and block in {8..256}: blocks are row-local.
+  const int L = block / 8;
+  const int groups = d / 8;
+  const int lane = threadIdx.x & 31;
+  const int64_t row_b0 = row_e0 / block;
+  for (int w = (threadIdx.x >> 5) * 32; w < groups; w += blockDim.x) {
+    const int tt = w + lane;
+    const bool valid = tt < groups;
+    float q[8];
+    if (valid) {
+      float4 a = *reinterpret_cast<const float4*>(srow + 8 * tt);
+      float4 b = *reinterpret_cast<const float4*>(srow + 8 * tt + 4);
+      q[0] = a.x; q[1] = a.y; q[2] = a.z; q[3] = a.w;
+      q[4] = b.x; q[5] = b.y; q[6] = b.z; q[7] = b.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = 0.0f;
+    }
+    quant8_store<BITS, MODE>(q, valid, L, row_e0 + 8 * tt, packed, scales, row_b0 + tt / L);
+  }
+}
+
+template <int BITS, int KIND, int V>
+__global__ void __launch_bounds__(256) hdequant_fast_kernel(
+    const uint8_t* __restrict__ packed, const float* __restrict__ scales, int d, float sqrtn,
+    float rsq, int dmode, const float* __restrict__ signs, int block, float* __restrict__ out) {
+  using W = whtr::Row<V>;
+  extern __shared__ __align__(16) float srow[];
+  const int64_t r = blockIdx.x;
+  const int64_t e0 = r * (int64_t)d;
+  const int t = threadIdx.x;
+  // scale of element i of the row: scales[(e0 + i) / block]; the row's
+  // first block and its offset in it, so the per-element index is 32-bit
+  const int64_t b0 = e0 / block;
+  const int off = (int)(e0 - b0 * block);
+  const float* srow_s = scales + b0;
+  const int bshift = (block & (block - 1)) == 0 ? __ffs(block) - 1 : -1;
+  float v[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = W::idxA(t, j);
+    float a = 0.0f;
+    if (i < d) {
+      const int k = off + i;
+      const float sc = __ldg(srow_s + (bshift >= 0 ? (k >> bshift) : k / block));
+      a = dequant_code<BITS, KIND>(raw_code<BITS>(packed, e0 + i), sc);
+    }
+    v[j] = a;
+  }
+  W::transform(v, srow);
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = W::idx(t, j);
+    if (i < d) out[e0 + i] = __fmul_rn(whtr::div_sqrtn(v[j], sqrtn, rsq, dmode), __ldg(signs + i));
+  }
+}
+
+template <int V>
+__global__ void __launch_bounds__(256) hrows_fast_kernel(const float* __restrict__ x, int d,
+                                                         float sqrtn, float rsq, int dmode,
+                                                         const float* __restrict__ signs,
+                                                         bool inverse, float* __restrict__ out) {
+  using W = whtr::Row<V>;
+  extern __shared__ __align__(16) float srow[];
+  const int64_t r = blockIdx.x;
+  const float* xr = x + r * d;
+  const int t = threadIdx.x;
+  float v[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = W::idxA(t, j);
+    float a = i < d ? __ldg(xr + i) : 0.0f;
+    if (!inverse && i < d) a = __fmul_rn(a, __ldg(signs + i));
+    v[j] = a;
+  }
+  W::transform(v, srow);  // ends with __syncthreads: in-place x == out is safe
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = W::idx(t, j);
+    if (i < d) {
+      float o = whtr::div_sqrtn(v[j], sqrtn, rsq, dmode);
+      if (inverse) o = __fmul_rn(o, __ldg(signs + i));
+      out[r * d + i] = o;
+    }
+  }
+}
+
 // ── host side ────────────────────────────────────────────────────────────────
 constexpr int kMaxHadamardN = 32768;
+
+// How the register transforms divide by fl32(sqrt(hn)) (whtr::div_sqrtn):
+// an exact reciprocal product for even powers of two, Markstein's corrected
+// product where it was checked equal to the IEEE quotient for every finite
+// float, else the IEEE division.
+int div_mode(int64_t hn) {
+  int l = 0;
+  while ((int64_t)1 << l < hn) ++l;
+  if (l % 2 == 0) return 1;
+  return (l >= 3 && l <= 15) ? 2 : 0;
+}
+
+// V of the register-resident transform for row length hn, or 0
+int wht_fast_v(int64_t hn) {
+  switch (hn) {
+    case 2048: return 8;
+    case 4096: return 16;
+    case 8192: return 32;
+    case 16384: return 64;
+  }
+  return 0;
+}
 
 bool pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
 int64_t pow2ceil(int64_t d) {
@@ -831,18 +998,33 @@ int quant_dispatch(const InT* x, int64_t n, int64_t row_len, int variant, int bl
   MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     kMaxHadamardN * (int)sizeof(float)));
   const bool fuse = vec_block(block) && d % block == 0 && aligned(packed, 8);
-  if (fuse) {
-    kern<<<(unsigned)rows, 256, smem, st>>>(x, (int)d, (int)hn, sqrtn, signs, block, true,
-                                            packed, scales, nullptr);
-    MXB_LAUNCH_CHECK();
-    return MXB_OK;
-  }
   const size_t rot_bytes = ((size_t)n * sizeof(float) + 255) & ~(size_t)255;
-  if (ws == nullptr || ws_bytes < rot_bytes) return MXB_E_WORKSPACE;
-  float* rot = static_cast<float*>(ws);
-  kern<<<(unsigned)rows, 256, smem, st>>>(x, (int)d, (int)hn, sqrtn, signs, block, false,
-                                          packed, scales, rot);
-  MXB_LAUNCH_CHECK();
+  if (!fuse && (ws == nullptr || ws_bytes < rot_bytes)) return MXB_E_WORKSPACE;
+  float* rot = fuse ? nullptr : static_cast<float*>(ws);
+  const int fv = wht_fast_v(hn);
+  if (fv) {
+    auto launch_fast = [&](auto kf, int V) -> int {
+      const size_t fs = ((size_t)hn + (size_t)(hn / 256) * (256 / V)) * sizeof(float);
+      MXB_CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fs));
+      kf<<<(unsigned)rows, 256, fs, st>>>(x, (int)d, sqrtn, 1.0f / sqrtn, div_mode(hn), signs,
+                                          block, fuse, packed, scales, rot);
+      MXB_LAUNCH_CHECK();
+      return MXB_OK;
+    };
+    int rc;
+    switch (fv) {
+      case 8: rc = launch_fast(hquant_fast_kernel<InT, BITS, MODE, 8>, 8); break;
+      case 16: rc = launch_fast(hquant_fast_kernel<InT, BITS, MODE, 16>, 16); break;
+      case 32: rc = launch_fast(hquant_fast_kernel<InT, BITS, MODE, 32>, 32); break;
+      default: rc = launch_fast(hquant_fast_kernel<InT, BITS, MODE, 64>, 64); break;
+    }
+    if (rc != MXB_OK || fuse) return rc;
+  } else {
+    kern<<<(unsigned)rows, 256, smem, st>>>(x, (int)d, (int)hn, sqrtn, signs, block, fuse,
+                                            packed, scales, rot);
+    MXB_LAUNCH_CHECK();
+    if (fuse) return MXB_OK;
+  }
   return quant_flat<float, BITS, MODE>(rot, n, block, packed, scales,
                                        static_cast<char*>(ws) + rot_bytes,
                                        ws_bytes - rot_bytes, st);
@@ -872,11 +1054,30 @@ int dequant_launch(const uint8_t* packed, const float* scales, int64_t n, int64_
     const int64_t hn = pow2ceil(d);
     if (d <= 0 || n % d != 0 || hn > kMaxHadamardN) return MXB_E_SHAPE;
     if (signs == nullptr) return MXB_E_ARG;
+    const float sqrtn = (float)sqrt((double)hn);
+    const int fv = wht_fast_v(hn);
+    if (fv) {
+      auto launch_fast = [&](auto kf, int V) -> int {
+        const size_t fs = ((size_t)hn + (size_t)(hn / 256) * (256 / V)) * sizeof(float);
+        MXB_CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)fs));
+        kf<<<(unsigned)(n / d), 256, fs, st>>>(packed, scales, (int)d, sqrtn, 1.0f / sqrtn,
+                                               div_mode(hn), signs, block, out);
+        MXB_LAUNCH_CHECK();
+        return MXB_OK;
+      };
+      switch (fv) {
+        case 8: return launch_fast(hdequant_fast_kernel<BITS, KIND, 8>, 8);
+        case 16: return launch_fast(hdequant_fast_kernel<BITS, KIND, 16>, 16);
+        case 32: return launch_fast(hdequant_fast_kernel<BITS, KIND, 32>, 32);
+        default: return launch_fast(hdequant_fast_kernel<BITS, KIND, 64>, 64);
+      }
+    }
     auto kern = hdequant_kernel<BITS, KIND>;
     MXB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       kMaxHadamardN * (int)sizeof(float)));
     kern<<<(unsigned)(n / d), 256, hn * sizeof(float), st>>>(
-        packed, scales, (int)d, (int)hn, (float)sqrt((double)hn), signs, block, out);
+        packed, scales, (int)d, (int)hn, sqrtn, signs, block, out);
     MXB_LAUNCH_CHECK();
     return MXB_OK;
   }
@@ -1127,10 +1328,29 @@ int mxb_hadamard_rows(const float* x, int64_t rows, int64_t d, const float* sign
   if (!x || !signs || !out) return MXB_E_ARG;
   const int64_t hn = pow2ceil(d);
   if (hn > kMaxHadamardN) return MXB_E_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float sqrtn = (float)sqrt((double)hn);
+  const int fv = wht_fast_v(hn);
+  if (fv) {
+    auto launch_fast = [&](auto kf, int V) -> int {
+      const size_t fs = ((size_t)hn + (size_t)(hn / 256) * (256 / V)) * sizeof(float);
+      MXB_CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fs));
+      kf<<<(unsigned)rows, 256, fs, st>>>(x, (int)d, sqrtn, 1.0f / sqrtn, div_mode(hn), signs,
+                                          inverse != 0, out);
+      MXB_LAUNCH_CHECK();
+      return MXB_OK;
+    };
+    switch (fv) {
+      case 8: return launch_fast(hrows_fast_kernel<8>, 8);
+      case 16: return launch_fast(hrows_fast_kernel<16>, 16);
+      case 32: return launch_fast(hrows_fast_kernel<32>, 32);
+      default: return launch_fast(hrows_fast_kernel<64>, 64);
+    }
+  }
   MXB_CUDA_TRY(cudaFuncSetAttribute(hrows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     kMaxHadamardN * (int)sizeof(float)));
-  hrows_kernel<<<(unsigned)rows, 256, hn * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
-      x, (int)d, (int)hn, (float)sqrt((double)hn), signs, inverse != 0, out);
+  hrows_kernel<<<(unsigned)rows, 256, hn * sizeof(float), st>>>(x, (int)d, (int)hn, sqrtn, signs,
+                                                              inverse != 0, out);
   MXB_LAUNCH_CHECK();
   return MXB_OK;
 }

@@ -359,7 +359,7 @@ def test_qgemm_kmajor_rejects_straddling_blocks():
 @pytest.mark.parametrize("K,N,block,x_dt", [
     (4096, 11008, 128, torch.bfloat16),   # configs[2]: 43 groups of 256 columns
     (1000, 640, 64, torch.float32),       # K not a multiple of 32, last group half wide
-    (333, 512, 256, torch.bfloat16),      # group wider than N
+    (328, 512, 256, torch.bfloat16),      # group wider than N
     (96, 256, 32, torch.float32),         # fewer units than SMs
     (8192, 3072, 1024, torch.bfloat16),   # one scale per group row
 ])
@@ -379,3 +379,25 @@ def test_streamed_gemv(M, dt, K, N, block, x_dt):
         y = ops.linear_wonly(x.cuda(), q._mx_packed, q._mx_scales, K, N, d, block)
         assert L.load().mxb_device_error(1) == 0
         _linear_check(y.cpu().numpy(), x.float().numpy(), wdq)
+
+
+@pytest.mark.parametrize("d", [2048, 3000, 4096, 8192, 12000, 16384])
+def test_register_wht_rows_bit_exact(d):
+    """Row lengths whose transform runs in registers (padded lengths 2048 ..
+    16384): rotation, unrotation, h quantize and h dequantize bit-identical
+    to the oracle's stage order (mxtorch.py:2811-2904, 1720-1736)."""
+    dt = get_mx_dtype("int4dh")
+    g = torch.Generator().manual_seed(d)
+    x = torch.randn(6, d, generator=g)
+    signs = mxb.sign_vector(d, dt.hadamard_seed).numpy()
+    rot = ops.hadamard_rows(x.cuda(), dt.hadamard_seed, inverse=False).cpu().numpy()
+    assert np.array_equal(_u32(rot), _u32(O.rotate(x.numpy(), signs)))
+    un = ops.hadamard_rows(x.cuda(), dt.hadamard_seed, inverse=True).cpu().numpy()
+    assert np.array_equal(_u32(un), _u32(O.unrotate(x.numpy(), signs)))
+    block = 128 if d % 128 == 0 else 8 if d % 8 == 0 else 100
+    q = mxb.mx_tensor.quantize(x.cuda(), dt, block)
+    p, s, _ = O.quantize(x.numpy(), 4, "int", block, True, signs)
+    assert np.array_equal(q._mx_packed.cpu().numpy(), p)
+    assert np.array_equal(_u32(q._mx_scales.cpu().numpy()), _u32(s))
+    ref = O.dequantize(p, s, 4, "int", (6, d), block, True, signs)
+    assert np.array_equal(_u32(q.dequantize().cpu().numpy()), _u32(ref))
