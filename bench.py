@@ -323,8 +323,9 @@ def run_ours(args, world, rank, local):
     n0 = lib.mxb_launch_count()
     step()
     launches = (lib.mxb_launch_count() - n0) * args.steps
-    # N > 1: eager steps (the NCCL ordering collective is not graph-captured here)
-    step_g = graphed(step, stream) if world == 1 else step
+    # the fused step (in-kernel barrier, no collective) replays from a CUDA
+    # graph; the NCCL all-gather variant runs eagerly
+    step_g = graphed(step, stream) if (world == 1 or fused) else step
     with Clocks(local) as clk:
         barrier(world)
         ts = time_steps(step_g, args.steps, flush, stream)
@@ -390,7 +391,8 @@ def run_ours(args, world, rank, local):
                                    "(configs[1])",
                        "global_batch": M,
                        "parallelism": f"N-sharded x{world}" + (
-                           ", output gather fused into the GEMM epilogue (peer stores)"
+                           ", output gather fused into the GEMM epilogue (peer stores, "
+                           "in-kernel completion barrier)"
                            if fused else (", NCCL all-gather" if world > 1 else "")
                            + (f" ({fuse_note})" if fuse_note else "")),
                        "l2": "flushed (256 MiB write) before every timed step"},

@@ -144,12 +144,45 @@ int mxb_qgemm_kmajor(const void* a_packed, const float* a_scales, int64_t a_nsca
                     workspace_bytes, true, stream);
 }
 
+static int qgemm_sharded_impl(const void* a_packed, const float* a_scales, int64_t a_nscales,
+                              const void* b_packed, const float* b_scales, int64_t b_nscales,
+                              int64_t M, int64_t K, int64_t N_local, int bits, int block,
+                              int64_t N_full, int64_t n_off, int nranks,
+                              void* const* out_words, float* const* out_scales,
+                              void* const* sync_blocks, int rank, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 int mxb_qgemm_sharded(const void* a_packed, const float* a_scales, int64_t a_nscales,
                       const void* b_packed, const float* b_scales, int64_t b_nscales,
                       int64_t M, int64_t K, int64_t N_local, int bits, int block,
                       int64_t N_full, int64_t n_off, int nranks, void* const* out_words,
                       float* const* out_scales, void* workspace, size_t workspace_bytes,
                       void* stream) {
+  return qgemm_sharded_impl(a_packed, a_scales, a_nscales, b_packed, b_scales, b_nscales, M, K,
+                            N_local, bits, block, N_full, n_off, nranks, out_words, out_scales,
+                            nullptr, 0, workspace, workspace_bytes, stream);
+}
+
+int mxb_qgemm_sharded_sync(const void* a_packed, const float* a_scales, int64_t a_nscales,
+                           const void* b_packed, const float* b_scales, int64_t b_nscales,
+                           int64_t M, int64_t K, int64_t N_local, int bits, int block,
+                           int64_t N_full, int64_t n_off, int nranks, int rank,
+                           void* const* out_words, float* const* out_scales,
+                           void* const* sync_blocks, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  if (!sync_blocks || rank < 0 || rank >= nranks) return MXB_E_ARG;
+  return qgemm_sharded_impl(a_packed, a_scales, a_nscales, b_packed, b_scales, b_nscales, M, K,
+                            N_local, bits, block, N_full, n_off, nranks, out_words, out_scales,
+                            sync_blocks, rank, workspace, workspace_bytes, stream);
+}
+
+static int qgemm_sharded_impl(const void* a_packed, const float* a_scales, int64_t a_nscales,
+                              const void* b_packed, const float* b_scales, int64_t b_nscales,
+                              int64_t M, int64_t K, int64_t N_local, int bits, int block,
+                              int64_t N_full, int64_t n_off, int nranks,
+                              void* const* out_words, float* const* out_scales,
+                              void* const* sync_blocks, int rank, void* workspace,
+                              size_t workspace_bytes, void* stream) {
   if (!int_bits(bits)) return MXB_E_DTYPE;
   if (M <= 0 || K <= 0 || N_local <= 0 || block <= 0) return MXB_E_SHAPE;
   if (nranks < 1 || nranks > kMaxPeers || !out_words || !out_scales) return MXB_E_ARG;
@@ -171,7 +204,12 @@ int mxb_qgemm_sharded(const void* a_packed, const float* a_scales, int64_t a_nsc
     if (!out_words[r] || !out_scales[r] || ((uintptr_t)out_words[r] & 15)) return MXB_E_ARG;
     q.words[r] = static_cast<uint32_t*>(out_words[r]);
     q.scales[r] = out_scales[r];
+    if (sync_blocks) {
+      if (!sync_blocks[r] || ((uintptr_t)sync_blocks[r] & 7)) return MXB_E_ARG;
+      q.sync[r] = static_cast<unsigned long long*>(sync_blocks[r]);
+    }
   }
+  q.rank = rank;
   const size_t need = align_up(tc_qgemm_workspace(M, K, N_local, bits));
   if (need && (!workspace || workspace_bytes < need)) return MXB_E_WORKSPACE;
   return tc_qgemm(a_packed, a_scales, b_packed, b_scales, M, K, N_local, bits, block, nullptr,

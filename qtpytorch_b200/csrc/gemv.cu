@@ -286,20 +286,12 @@ int launch_wide(int mt, int lb, dim3 grid, const XT* x, int M, int K, const uint
 namespace mxb {
 
 GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,
-                   const void* w, const void* y, int x_dtype, const void* x, bool allow_tma) {
+                   const void* w, const void* y, int x_dtype, const void* x) {
   GemvPlan p{false, 0, 0, 0};
-  if (x_dtype < 0) {
-    // workspace query (pointers unknown): the largest of the bf16 and fp32
-    // plans, with and without the streamed kernel (which needs 16-byte
-    // aligned weights)
-    GemvPlan best = gemv_plan(M, K, N, bits, kind, block, w, y, MXB_BF16, nullptr, true);
-    const int dts[2] = {MXB_BF16, MXB_F32};
-    for (int t = 0; t < 2; ++t)
-      for (int a = 0; a < 2; ++a) {
-        GemvPlan q = gemv_plan(M, K, N, bits, kind, block, w, y, dts[t], nullptr, a == 1);
-        if (q.ws_bytes > best.ws_bytes) best = q;
-      }
-    return best;
+  if (x_dtype < 0) {  // workspace query: the larger of the bf16 and fp32 plans
+    GemvPlan a = gemv_plan(M, K, N, bits, kind, block, w, y, MXB_BF16, nullptr);
+    GemvPlan b = gemv_plan(M, K, N, bits, kind, block, w, y, MXB_F32, nullptr);
+    return a.ws_bytes >= b.ws_bytes ? a : b;
   }
   if (M >= 1 && K >= 1 && ((uintptr_t)y % 16) == 0 &&
       tc_dec_eligible(x, x_dtype, M, K, w, N, bits, kind, block)) {
@@ -311,16 +303,6 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
     p.krows = kc;
     p.max_krows = kDecMaxKc;
     p.ws_bytes = splits > 1 ? (size_t)splits * M * N * sizeof(float) : 0;
-    return p;
-  }
-  if (allow_tma && tma_gemv_eligible(x, x_dtype, M, K, w, N, bits, kind, block,
-                        static_cast<const float*>(y))) {
-    p.ok = true;
-    p.kernel = 5;
-    p.splits = 1;
-    p.krows = 0;  // the run geometry is the kernel's own; nothing to lengthen
-    p.max_krows = 0;
-    p.ws_bytes = tma_gemv_workspace(M, K, N, bits, block);
     return p;
   }
   if (M < 1 || M > 16 || K < 1 || N < kCols) return p;
@@ -373,9 +355,7 @@ int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_
   dim3 grid((unsigned)cdiv(N, kCtaCols), (unsigned)plan.splits);
   const uint8_t* W = static_cast<const uint8_t*>(w);
   int rc;
-  if (plan.kernel == 5) {
-    return tma_gemv(x, x_dtype, M, K, w, ws, N, bits, block, y, partial, plan.ws_bytes, st);
-  } else if (plan.kernel == 4) {
+  if (plan.kernel == 4) {
     if (x_dtype != MXB_BF16 || plan.krows > plan.max_krows) return MXB_E_ARG;
     rc = tc_wonly_dec(x, M, K, w, ws, N, bits, block, plan.krows, plan.splits,
                       plan.splits > 1 ? partial : y, st);

@@ -29,16 +29,14 @@ struct GemvPlan {
   int krows;        // rows of K per split
   size_t ws_bytes;  // partial-sum workspace
   int kernel = 0;   // 0: 8 columns per thread, any code width; 1: wide loads (int4/int8);
-                    // 4: tcgen05 decode kernel (bf16 x, integer codes, 3 <= M <= 32);
-                    // 5: streamed TMA GEMV (int4 / int8, M <= 2)
+                    // 4: tcgen05 decode kernel (bf16 x, integer codes, 3 <= M <= 32)
   int lb = 0;       // kernel 1: code bytes per thread and row (4, 8 or 16)
   int max_krows = 0;  // largest rows per split the kernel accepts
 };
 // x_dtype < 0: the dtype is not known yet (workspace queries); the plan then
 // covers the largest workspace either activation dtype may need.
 GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int block,
-                   const void* w, const void* y, int x_dtype, const void* x,
-                   bool allow_tma = true);
+                   const void* w, const void* y, int x_dtype, const void* x);
 int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_t K,
              const void* w, const float* ws, int64_t N, int bits, int kind, int block,
              float* y, float* partial, cudaStream_t st);
@@ -55,7 +53,16 @@ struct QOut {
   int count;
   int row_stride;
   int col_off;
+  // completion barrier across the ranks inside the kernel (sync[0] != null):
+  // sync[r] is rank r's barrier word block (SyncBlock), this rank's own
+  // included; `rank` indexes this rank
+  unsigned long long* sync[kMaxPeers];
+  int rank;
 };
+// Layout of a rank's barrier block (zeroed once by the caller): [0] the
+// count of this launch's finished CTAs, [1] this rank's call counter,
+// [8 + r] the call counter rank r last signalled to this rank.
+constexpr int kSyncWords = 16;
 bool tc_qgemm_eligible(int64_t M, int64_t K, int64_t N, int bits, int block, bool sa_ok,
                        bool sb_ok, const void* a, const void* b, const float* c);
 size_t tc_qgemm_workspace(int64_t M, int64_t K, int64_t N, int bits);
@@ -81,12 +88,4 @@ bool tc_dec_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const voi
 void tc_dec_plan(int64_t K, int64_t N, int* splits, int* kc);
 int tc_wonly_dec(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
                  int bits, int block, int kc, int splits, float* out, cudaStream_t st);
-// streamed GEMV (M <= 2, int4 / int8 codes): partial rows in `part`
-bool tma_gemv_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
-                       int64_t N, int bits, int kind, int block, const float* y);
-size_t tma_gemv_workspace(int64_t M, int64_t K, int64_t N, int bits, int block);
-int tma_gemv(const void* x, int x_dtype, int64_t M, int64_t K, const void* w, const float* ws,
-             int64_t N, int bits, int block, float* y, float* part, size_t part_bytes,
-             cudaStream_t st);
-
 }  // namespace mxb

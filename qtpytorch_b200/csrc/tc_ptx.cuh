@@ -24,6 +24,7 @@ enum DeviceError : int {
   kErrTimeoutTmemFull = 3,
   kErrTimeoutTmemEmpty = 4,
   kErrTimeoutDone = 5,
+  kErrTimeoutPeer = 6,  // a peer rank never signalled the cross-rank barrier
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

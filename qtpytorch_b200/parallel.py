@@ -110,6 +110,28 @@ class PeerOutputs:
         lib = L.load()
         self._opened = []
         self.sets = []
+        # the in-kernel barrier's block of this rank (zeroed once), mapped by
+        # every peer like the outputs
+        self.sync = torch.zeros(16, dtype=torch.int64, device=dev)
+        mine = self._share(self.sync)
+        allh = [None] * world
+        if world > 1:
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh[0] = mine
+        ptr_sync = []
+        for r in range(world):
+            if r == rank:
+                ptr_sync.append(self.sync.data_ptr())
+                continue
+            handle, off = allh[r]
+            base = C.c_void_p()
+            with torch.cuda.device(dev):
+                rc = lib.mxb_ipc_open(handle, len(handle), C.byref(base))
+            L.check(rc, "mxb_ipc_open")
+            self._opened.append(base.value)
+            ptr_sync.append(base.value + off)
+        self.ptr_sync = (C.c_void_p * world)(*ptr_sync)
         for _ in range(2):
             words = torch.empty(M * N_full // 2, dtype=torch.int32, device=dev)
             scales = torch.empty(M * N_full // block, dtype=torch.float32, device=dev)
@@ -172,13 +194,16 @@ class PeerOutputs:
 
 
 def sharded_qgemm_fused(qa: mx_tensor, w: ShardedQGemmWeight, peers: PeerOutputs,
-                        group=None) -> mx_tensor:
+                        group=None, in_kernel_barrier: bool = True) -> mx_tensor:
     """C = A @ B with B column-sharded, the output all-gather fused into the
     GEMM kernel: every rank's epilogue writes its tiles' int16d codes and
-    scales straight into all ranks' full-width outputs (mxb_qgemm_sharded),
-    then a one-element all-reduce on the stream orders the ranks' writes
-    before any rank reads.  Same result as ``sharded_qgemm``; needs the
-    tcgen05 shapes (M, K and every shard a multiple of 128, block 128)."""
+    scales straight into all ranks' full-width outputs.  The ranks' writes
+    are ordered before any rank reads either by a barrier inside the kernel
+    (``in_kernel_barrier``, mxb_qgemm_sharded_sync: no collective follows,
+    and the step can be captured in a CUDA graph) or by a one-element
+    all-reduce on the stream after it (mxb_qgemm_sharded).  Same result as
+    ``sharded_qgemm``; needs the tcgen05 shapes (M, K and every shard a
+    multiple of 128, block 128)."""
     from . import _lib as L
     import ctypes as C
     M, K = qa._mx_orig_shape
@@ -194,14 +219,22 @@ def sharded_qgemm_fused(qa: mx_tensor, w: ShardedQGemmWeight, peers: PeerOutputs
     ws = L.workspace(wsb, dev)
     out = peers.next()
     with torch.cuda.device(dev):
-        rc = lib.mxb_qgemm_sharded(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales),
-                                   qa._mx_scales.numel(), L.ptr(w.codes), L.ptr(w.scales),
-                                   w.scales.numel(), M, K, nl, w.dtype.bits, w.block, w.N,
-                                   w.n0, w.world, C.cast(out["ptr_w"], C.c_void_p),
-                                   C.cast(out["ptr_s"], C.c_void_p), L.ptr(ws), wsb,
-                                   L.stream_of(dev))
+        if in_kernel_barrier:
+            rc = lib.mxb_qgemm_sharded_sync(
+                L.ptr(qa._mx_packed), L.ptr(qa._mx_scales), qa._mx_scales.numel(),
+                L.ptr(w.codes), L.ptr(w.scales), w.scales.numel(), M, K, nl, w.dtype.bits,
+                w.block, w.N, w.n0, w.world, w.rank, C.cast(out["ptr_w"], C.c_void_p),
+                C.cast(out["ptr_s"], C.c_void_p), C.cast(peers.ptr_sync, C.c_void_p),
+                L.ptr(ws), wsb, L.stream_of(dev))
+        else:
+            rc = lib.mxb_qgemm_sharded(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales),
+                                       qa._mx_scales.numel(), L.ptr(w.codes), L.ptr(w.scales),
+                                       w.scales.numel(), M, K, nl, w.dtype.bits, w.block, w.N,
+                                       w.n0, w.world, C.cast(out["ptr_w"], C.c_void_p),
+                                       C.cast(out["ptr_s"], C.c_void_p), L.ptr(ws), wsb,
+                                       L.stream_of(dev))
     L.check(rc, f"mxb_qgemm_sharded({M}x{K}x{nl} of {w.N})")
-    if w.world > 1:
+    if w.world > 1 and not in_kernel_barrier:
         flag = torch.zeros(1, device=dev)
         dist.all_reduce(flag, group=group)  # every rank's kernel (and its peer stores) done
     return mx_tensor(out["words"], out["scales"], out_dt, torch.Size([M, w.N]), M * w.N, w.block)

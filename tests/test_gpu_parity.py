@@ -363,11 +363,10 @@ def test_qgemm_kmajor_rejects_straddling_blocks():
     (96, 256, 32, torch.float32),         # fewer units than SMs
     (8192, 3072, 1024, torch.bfloat16),   # one scale per group row
 ])
-def test_streamed_gemv(M, dt, K, N, block, x_dt):
-    """The streamed TMA GEMV (M <= 2, int4 / int8): runs that cross group
-    boundaries, ragged K, half-width last groups, block sizes below and
-    above the 256-column group, fp32 and bf16 x; and a second call that
-    reuses the workspace."""
+def test_decode_gemv_shapes(M, dt, K, N, block, x_dt):
+    """The decode GEMV (M <= 2, int4 / int8) at the configs[2] shape, ragged
+    K, a 640-wide N, small K, blocks from 32 to 1024, fp32 and bf16 x; and a
+    second call that reuses the workspace."""
     d = get_mx_dtype(dt)
     g = torch.Generator().manual_seed(K + N + M)
     w = torch.randn(K, N, generator=g) * 0.02
