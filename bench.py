@@ -241,7 +241,7 @@ def run_ours(args, world, rank, local):
     def flush():
         flush_buf.zero_()
 
-    if args.only in ("gemv1", "gemv16", "wo2048", "quant", "dequant"):
+    if args.only in ("gemv1", "gemv16", "wo2048", "quant", "dequant", "h"):
         print(json.dumps(run_extras(args, dev, flush, torch.cuda.current_stream(dev), hbm, bf16)))
         return
     if args.only == "sweep":  # the full configs[4] sweep (a few minutes), one JSON line
@@ -392,7 +392,7 @@ def run_ours(args, world, rank, local):
                        "global_batch": M,
                        "parallelism": f"N-sharded x{world}" + (
                            ", output gather fused into the GEMM epilogue (peer stores, "
-                           "in-kernel completion barrier)"
+                           "completion barrier kernel over peer flags)"
                            if fused else (", NCCL all-gather" if world > 1 else "")
                            + (f" ({fuse_note})" if fuse_note else "")),
                        "l2": "flushed (256 MiB write) before every timed step"},
@@ -576,6 +576,17 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
             ops.quantize(x, mxb.int4d, 128)
         torch.cuda.synchronize()
         return {"only": "quant"}
+    if args.only == "h":  # profiling case: int4dh quantize / dequantize of W^T 8192 x 8192
+        # and the row unrotation of y 4096 x 8192
+        dt = mxb.get_mx_dtype("int4dh")
+        w = torch.randn(8192, 8192, device=dev) * 0.02
+        y = torch.randn(4096, 8192, device=dev)
+        for _ in range(3 + args.steps):
+            p_, s_, n_ = ops.quantize(w, dt, 128)
+            ops.dequantize(p_, s_, dt, n_, 128, (8192, 8192))
+            ops.hadamard_rows(y, dt.hadamard_seed, True)
+        torch.cuda.synchronize()
+        return {"only": "h"}
     if args.only == "dequant":  # profiling case: int4d dequantize of 2^26 values
         x = torch.randn(1 << 26, device=dev)
         p_, s_, _ = ops.quantize(x, mxb.int4d, 128)
@@ -734,7 +745,7 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="N > 1: output gather fused into the GEMM kernel, or NCCL all-gather")
-    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant", "dequant", "sweep"],
+    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant", "dequant", "h", "sweep"],
                     help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -243,18 +243,18 @@ int mxb_qgemm_sharded(const void* a_packed, const float* a_scales, int64_t a_nsc
                       void* stream);
 
 /*
- * mxb_qgemm_sharded with the ranks' completion barrier inside the kernel,
- * so no collective follows the launch: when the kernel ends, every rank's
- * stores into this rank's output are complete.  sync_blocks[r] is rank r's
- * 16-word (128-byte, 8-byte aligned) barrier block, this rank's own
- * (sync_blocks[rank]) included, zeroed once before the first call and left
- * to the library afterwards; every rank makes the same sequence of calls.
- * The last CTA of each rank's launch signals the call to every rank with a
- * system-scope store and waits (at most 2 s, then the device error word
- * holds 6 and the output is invalid) for all ranks' signals.  The counters
- * live on the device, so a captured CUDA graph replays correctly.  Other
- * arguments and result as mxb_qgemm_sharded.  No counterpart in the
- * reference.
+ * mxb_qgemm_sharded followed on the stream by the library's own cross-rank
+ * completion barrier, so no collective is needed: when the call's work on
+ * the stream is done, every rank's stores into this rank's output are
+ * complete.  sync_blocks[r] is rank r's 16-word (128-byte, 8-byte aligned)
+ * barrier block, this rank's own (sync_blocks[rank]) included, zeroed once
+ * before the first call and left to the library afterwards; every rank
+ * makes the same sequence of calls.  A one-thread kernel after the matmul
+ * signals the call to every rank with a system-scope store and waits (at
+ * most 2 s, then the device error word holds 6 and the output is invalid)
+ * for all ranks' signals.  The counters live on the device, so a captured
+ * CUDA graph replays correctly.  Other arguments and result as
+ * mxb_qgemm_sharded.  No counterpart in the reference.
  */
 int mxb_qgemm_sharded_sync(const void* a_packed, const float* a_scales, int64_t a_nscales,
                            const void* b_packed, const float* b_scales, int64_t b_nscales,

@@ -67,18 +67,18 @@ struct Bars {
 static_assert(sizeof(Bars) <= kBarsBytes, "barrier block overflows its shared-memory slot");
 static_assert(offsetof(Bars, sbw) % 16 == 0, "float4 reads of sbw need 16-byte alignment");
 
-// The last CTA of this rank's launch to finish raises this rank's call
-// counter, signals it to every rank (system-scope release stores into their
-// barrier blocks) and waits, bounded by kWaitLimitNs, until every rank has
-// signalled the same call: the kernel ends only when all ranks' stores into
-// this rank's output are complete.  The counters advance in step on every
-// rank (one per call), so the protocol needs no host state and replays
-// under a CUDA graph.  A wait that gives up records kErrTimeoutPeer.
-__device__ __noinline__ void cross_rank_barrier(const QOut& q) {
+// Cross-rank completion barrier, launched right after a rank's sharded
+// matmul on the same stream (so every store of that kernel, over NVLink
+// included, is complete when it runs): one thread raises this rank's call
+// counter, signals it to every rank with a system-scope release store into
+// their barrier blocks and waits, bounded by kWaitLimitNs, until every rank
+// has signalled the same call.  The counters advance in step on every rank
+// (one per call) and live on the device, so the protocol needs no host
+// state and replays under a CUDA graph.  A wait that gives up records
+// kErrTimeoutPeer.
+__global__ void __launch_bounds__(32) cross_rank_barrier_kernel(const __grid_constant__ QOut q) {
+  if (threadIdx.x != 0) return;
   unsigned long long* mine = q.sync[q.rank];
-  const unsigned long long prev = atomicAdd(mine, 1ull);
-  if (prev != (unsigned long long)(gridDim.x * gridDim.y) - 1) return;
-  atomicExch(mine, 0ull);  // reset the CTA count for the next call
   __threadfence_system();
   const unsigned long long call = mine[1] + 1;
   mine[1] = call;
@@ -97,7 +97,7 @@ __device__ __noinline__ void cross_rank_barrier(const QOut& q) {
         atomicCAS(&g_mxb_device_error, 0, kErrTimeoutPeer);
         return;
       }
-      __nanosleep(100);
+      __nanosleep(64);
     }
   }
 }
@@ -308,25 +308,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // The CTA waits only for its staging buffer to be read; the row copies
       // (over NVLink for peers) finish while the next tiles compute, and are
-      // complete when the kernel is, which the caller's post-launch barrier
-      // orders before any rank reads.  With the in-kernel barrier the copies
-      // must be complete (not only read) before the CTA counts as done.
-      if (lane < 2) {
-        if (qout.sync[0] != nullptr)
-          asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-        else
-          bulk_wait_read();
-      }
+      // complete when the kernel is, which the post-launch barrier (the
+      // cross-rank barrier kernel, or a collective) orders before any rank
+      // reads.
+      if (lane < 2) bulk_wait_read();
     }
   }
-  if (qout.sync[0] != nullptr) {
-    // every store of this CTA (bulk copies: async proxy; scales: generic)
-    // visible system-wide before the CTA is counted
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    __threadfence_system();
-  }
   __syncthreads();
-  if (qout.sync[0] != nullptr && threadIdx.x == 0) cross_rank_barrier(qout);
   if (warp == 1) {
     mbar_wait(&bars->done, 0, kErrTimeoutDone);
     __syncwarp();
@@ -532,6 +520,10 @@ int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int
   kern<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C,
                                            qout ? *qout : none);
   MXB_LAUNCH_CHECK();
+  if (qout && qout->sync[0] != nullptr) {
+    cross_rank_barrier_kernel<<<1, 32, 0, st>>>(*qout);
+    MXB_LAUNCH_CHECK();
+  }
   return MXB_OK;
 }
 

@@ -53,15 +53,15 @@ struct QOut {
   int count;
   int row_stride;
   int col_off;
-  // completion barrier across the ranks inside the kernel (sync[0] != null):
-  // sync[r] is rank r's barrier word block (SyncBlock), this rank's own
-  // included; `rank` indexes this rank
+  // completion barrier across the ranks after the kernel (sync[0] != null):
+  // sync[r] is rank r's barrier block, this rank's own included; `rank`
+  // indexes this rank
   unsigned long long* sync[kMaxPeers];
   int rank;
 };
-// Layout of a rank's barrier block (zeroed once by the caller): [0] the
-// count of this launch's finished CTAs, [1] this rank's call counter,
-// [8 + r] the call counter rank r last signalled to this rank.
+// Layout of a rank's barrier block (zeroed once by the caller): [1] this
+// rank's call counter, [8 + r] the call counter rank r last signalled to
+// this rank.
 constexpr int kSyncWords = 16;
 bool tc_qgemm_eligible(int64_t M, int64_t K, int64_t N, int bits, int block, bool sa_ok,
                        bool sb_ok, const void* a, const void* b, const float* c);

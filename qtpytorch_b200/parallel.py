@@ -198,10 +198,10 @@ def sharded_qgemm_fused(qa: mx_tensor, w: ShardedQGemmWeight, peers: PeerOutputs
     """C = A @ B with B column-sharded, the output all-gather fused into the
     GEMM kernel: every rank's epilogue writes its tiles' int16d codes and
     scales straight into all ranks' full-width outputs.  The ranks' writes
-    are ordered before any rank reads either by a barrier inside the kernel
-    (``in_kernel_barrier``, mxb_qgemm_sharded_sync: no collective follows,
-    and the step can be captured in a CUDA graph) or by a one-element
-    all-reduce on the stream after it (mxb_qgemm_sharded).  Same result as
+    are ordered before any rank reads either by the library's barrier kernel
+    over peer-mapped flags (``in_kernel_barrier``, mxb_qgemm_sharded_sync:
+    no collective, and the step can be captured in a CUDA graph) or by a
+    one-element all-reduce on the stream after it (mxb_qgemm_sharded).  Same result as
     ``sharded_qgemm``; needs the tcgen05 shapes (M, K and every shard a
     multiple of 128, block 128)."""
     from . import _lib as L
