@@ -249,6 +249,16 @@ def run_ours(args, world, rank, local):
                                              max(3, min(args.steps, 10)))}))
         return
 
+    if args.only == "gemm8192":  # traffic case: the GEMM at 8192^3 (output > L2), untimed
+        g = torch.Generator().manual_seed(0)
+        qa8 = mxb.mx_tensor.quantize(torch.randn(8192, 8192, generator=g).to(dev), mxb.int8d, BLOCK)
+        qb8 = mxb.mx_tensor.quantize(torch.randn(8192, 8192, generator=g).to(dev), mxb.int8d, BLOCK)
+        for _ in range(3 + args.steps):
+            qa8 @ qb8
+        torch.cuda.synchronize()
+        print(json.dumps({"only": "gemm8192", "device_error": lib.mxb_device_error(1)}))
+        return
+
     a_h, b_h = make_inputs()
     qa = mxb.mx_tensor.quantize(a_h.to(dev), mxb.int8d, BLOCK)
     qb = mxb.mx_tensor.quantize(b_h.to(dev), mxb.int8d, BLOCK)
@@ -745,7 +755,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="N > 1: output gather fused into the GEMM kernel, or NCCL all-gather")
-    ap.add_argument("--only", default=None, choices=["gemm", "gemv1", "gemv16", "wo2048", "quant", "dequant", "h", "sweep"],
+    ap.add_argument("--only", default=None, choices=["gemm", "gemm8192", "gemv1", "gemv16", "wo2048", "quant", "dequant", "h",
+                             "sweep"],
                     help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:

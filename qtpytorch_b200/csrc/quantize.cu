@@ -769,10 +769,37 @@ __global__ void __launch_bounds__(256) hquant_fast_kernel(
   const InT* xr = x + r * d;
   const int t = threadIdx.x;
   float v[V];
+  if (W::kPhaseC && W::kG >= 8 && d % W::kG == 0 && ((uintptr_t)xr & 15) == 0) {
+    // the row in runs of kG consecutive elements (16-byte loads), times the
+    // signs, then to the phase-A layout through shared memory
 #pragma unroll
-  for (int j = 0; j < V; ++j) {
-    const int i = W::idxA(t, j);
-    v[j] = i < d ? __fmul_rn(load_as_f32(xr, i), __ldg(signs + i)) : 0.0f;
+    for (int q = 0; q < W::kRuns; ++q) {
+      const int i0 = W::idx(t, q * W::kG);
+#pragma unroll
+      for (int c8 = 0; c8 < W::kG / 8; ++c8) {
+        float a[8];
+        if (i0 < d) {
+          load8<InT>(xr, i0 + 8 * c8, d, true, a);
+          const float4 s0 = __ldg(reinterpret_cast<const float4*>(signs + i0 + 8 * c8));
+          const float4 s1 = __ldg(reinterpret_cast<const float4*>(signs + i0 + 8 * c8) + 1);
+          const float sg[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+          for (int c = 0; c < 8; ++c) a[c] = __fmul_rn(a[c], sg[c]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) a[c] = 0.0f;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) v[q * W::kG + 8 * c8 + c] = a[c];
+      }
+    }
+    if constexpr (W::kPhaseC) W::from_runs(v, srow);
+  } else {
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int i = W::idxA(t, j);
+      v[j] = i < d ? __fmul_rn(load_as_f32(xr, i), __ldg(signs + i)) : 0.0f;
+    }
   }
   W::transform(v, srow);
 #pragma unroll
@@ -847,16 +874,61 @@ __global__ void __launch_bounds__(256) hdequant_fast_kernel(
   const float* srow_s = scales + b0;
   const int bshift = (block & (block - 1)) == 0 ? __ffs(block) - 1 : -1;
   float v[V];
+  constexpr int RB = W::kG * BITS / 8;  // bytes of one run's codes
+  if (W::kPhaseC && BITS <= 8 && d % W::kG == 0 && (e0 * BITS / 8) % RB == 0 &&
+      ((uintptr_t)packed % RB) == 0) {
+    // each run's codes in one load, decoded in registers, then to the
+    // phase-A layout through shared memory
 #pragma unroll
-  for (int j = 0; j < V; ++j) {
-    const int i = W::idxA(t, j);
-    float a = 0.0f;
-    if (i < d) {
-      const int k = off + i;
-      const float sc = __ldg(srow_s + (bshift >= 0 ? (k >> bshift) : k / block));
-      a = dequant_code<BITS, KIND>(raw_code<BITS>(packed, e0 + i), sc);
+    for (int q = 0; q < W::kRuns; ++q) {
+      const int i0 = W::idx(t, q * W::kG);
+      uint64_t word = 0;
+      if (i0 < d) {
+        const uint8_t* p = packed + (e0 + i0) * BITS / 8;
+        if constexpr (RB == 16) {
+          // 16 int8 codes: the low 8 here; the run loop below reads the rest
+          word = __ldg(reinterpret_cast<const unsigned long long*>(p));
+        } else if constexpr (RB == 8) {
+          word = __ldg(reinterpret_cast<const unsigned long long*>(p));
+        } else if constexpr (RB == 4) {
+          word = __ldg(reinterpret_cast<const uint32_t*>(p));
+        } else if constexpr (RB == 2) {
+          word = __ldg(reinterpret_cast<const uint16_t*>(p));
+        } else {
+          word = __ldg(p);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < W::kG; ++c) {
+        float a = 0.0f;
+        if (i0 < d) {
+          const int k = off + i0 + c;
+          const float sc = __ldg(srow_s + (bshift >= 0 ? (k >> bshift) : k / block));
+          uint32_t raw;
+          if constexpr (RB == 16) {
+            raw = c < 8 ? (uint32_t)(word >> (8 * c)) & 0xffu
+                        : (uint32_t)__ldg(packed + (e0 + i0 + c));
+          } else {
+            raw = (uint32_t)(word >> (c * BITS)) & ((1u << BITS) - 1u);
+          }
+          a = dequant_code<BITS, KIND>(raw, sc);
+        }
+        v[q * W::kG + c] = a;
+      }
     }
-    v[j] = a;
+    if constexpr (W::kPhaseC) W::from_runs(v, srow);
+  } else {
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int i = W::idxA(t, j);
+      float a = 0.0f;
+      if (i < d) {
+        const int k = off + i;
+        const float sc = __ldg(srow_s + (bshift >= 0 ? (k >> bshift) : k / block));
+        a = dequant_code<BITS, KIND>(raw_code<BITS>(packed, e0 + i), sc);
+      }
+      v[j] = a;
+    }
   }
   W::transform(v, srow);
 #pragma unroll
@@ -877,12 +949,38 @@ __global__ void __launch_bounds__(256) hrows_fast_kernel(const float* __restrict
   const float* xr = x + r * d;
   const int t = threadIdx.x;
   float v[V];
+  if (W::kPhaseC && d % W::kG == 0 && ((uintptr_t)xr & 15) == 0) {
+    // the row in runs of kG consecutive elements (16-byte loads), then to
+    // the phase-A layout through shared memory
 #pragma unroll
-  for (int j = 0; j < V; ++j) {
-    const int i = W::idxA(t, j);
-    float a = i < d ? __ldg(xr + i) : 0.0f;
-    if (!inverse && i < d) a = __fmul_rn(a, __ldg(signs + i));
-    v[j] = a;
+    for (int q = 0; q < W::kRuns; ++q) {
+      const int i0 = W::idx(t, q * W::kG);
+#pragma unroll
+      for (int c4 = 0; c4 < W::kG / 4; ++c4) {
+        float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i0 < d) {
+          a = __ldg(reinterpret_cast<const float4*>(xr + i0) + c4);
+          if (!inverse) {
+            const float4 sg = __ldg(reinterpret_cast<const float4*>(signs + i0) + c4);
+            a = make_float4(__fmul_rn(a.x, sg.x), __fmul_rn(a.y, sg.y), __fmul_rn(a.z, sg.z),
+                            __fmul_rn(a.w, sg.w));
+          }
+        }
+        v[q * W::kG + 4 * c4] = a.x;
+        v[q * W::kG + 4 * c4 + 1] = a.y;
+        v[q * W::kG + 4 * c4 + 2] = a.z;
+        v[q * W::kG + 4 * c4 + 3] = a.w;
+      }
+    }
+    if constexpr (W::kPhaseC) W::from_runs(v, srow);
+  } else {
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int i = W::idxA(t, j);
+      float a = i < d ? __ldg(xr + i) : 0.0f;
+      if (!inverse && i < d) a = __fmul_rn(a, __ldg(signs + i));
+      v[j] = a;
+    }
   }
   W::transform(v, srow);  // ends with __syncthreads: in-place x == out is safe
 #pragma unroll

@@ -64,6 +64,27 @@ struct Row {
     }
   }
 
+  // Runs (the final layout) -> phase-A slots, through shared memory, for
+  // rows that are loaded in runs of consecutive elements (vector loads).
+  // Begins and ends with __syncthreads.
+  __device__ static void from_runs(float (&v)[V], float* s) {
+    static_assert(kPhaseC, "runs exist for V >= 16");
+    const int t = threadIdx.x;
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kRuns; ++r) {
+      float4* p = reinterpret_cast<float4*>(s + pad((t + 256 * r) << kLB));
+#pragma unroll
+      for (int q = 0; q < kG / 4; ++q)
+        p[q] = make_float4(v[r * kG + 4 * q], v[r * kG + 4 * q + 1], v[r * kG + 4 * q + 2],
+                           v[r * kG + 4 * q + 3]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < V; ++j) v[j] = s[pad(idxA(t, j))];
+    __syncthreads();
+  }
+
   // v: phase-A slots on entry, final slots (idx) on exit.  `s` holds
   // kSmemFloats; the function begins and ends with __syncthreads.
   __device__ static void transform(float (&v)[V], float* s) {

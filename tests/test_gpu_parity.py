@@ -380,23 +380,30 @@ def test_decode_gemv_shapes(M, dt, K, N, block, x_dt):
         _linear_check(y.cpu().numpy(), x.float().numpy(), wdq)
 
 
-@pytest.mark.parametrize("d", [2048, 3000, 4096, 8192, 12000, 16384])
-def test_register_wht_rows_bit_exact(d):
+@pytest.mark.parametrize("d,dtn", [(2048, "int4dh"), (3000, "int4dh"), (4096, "int4dh"),
+                                   (8192, "int4dh"), (12000, "int4dh"), (16384, "int4dh"),
+                                   (4096, "int8dh"), (8192, "int8dh"), (8192, "int2dh"),
+                                   (4096, "float4dh"), (16384, "int1dh")])
+def test_register_wht_rows_bit_exact(d, dtn):
     """Row lengths whose transform runs in registers (padded lengths 2048 ..
-    16384): rotation, unrotation, h quantize and h dequantize bit-identical
-    to the oracle's stage order (mxtorch.py:2811-2904, 1720-1736)."""
-    dt = get_mx_dtype("int4dh")
+    16384), rows loaded element-wise or in runs: rotation, unrotation, h
+    quantize and h dequantize bit-identical to the oracle's stage order
+    (mxtorch.py:2811-2904, 1720-1736)."""
+    dt = get_mx_dtype(dtn)
     g = torch.Generator().manual_seed(d)
     x = torch.randn(6, d, generator=g)
+    if dtn == "int8dh":  # bf16 rows through the quantizer's run loads
+        x = x.bfloat16().float()
     signs = mxb.sign_vector(d, dt.hadamard_seed).numpy()
     rot = ops.hadamard_rows(x.cuda(), dt.hadamard_seed, inverse=False).cpu().numpy()
     assert np.array_equal(_u32(rot), _u32(O.rotate(x.numpy(), signs)))
     un = ops.hadamard_rows(x.cuda(), dt.hadamard_seed, inverse=True).cpu().numpy()
     assert np.array_equal(_u32(un), _u32(O.unrotate(x.numpy(), signs)))
     block = 128 if d % 128 == 0 else 8 if d % 8 == 0 else 100
-    q = mxb.mx_tensor.quantize(x.cuda(), dt, block)
-    p, s, _ = O.quantize(x.numpy(), 4, "int", block, True, signs)
+    xq = x.bfloat16() if dtn == "int8dh" else x  # exact: x holds bf16 values there
+    q = mxb.mx_tensor.quantize(xq.cuda(), dt, block)
+    p, s, _ = O.quantize(x.numpy(), dt.bits, dt.kind, block, True, signs)
     assert np.array_equal(q._mx_packed.cpu().numpy(), p)
     assert np.array_equal(_u32(q._mx_scales.cpu().numpy()), _u32(s))
-    ref = O.dequantize(p, s, 4, "int", (6, d), block, True, signs)
+    ref = O.dequantize(p, s, dt.bits, dt.kind, (6, d), block, True, signs)
     assert np.array_equal(_u32(q.dequantize().cpu().numpy()), _u32(ref))
