@@ -408,6 +408,9 @@ def run_ours(args, world, rank, local):
                        "l2": "flushed (256 MiB write) before every timed step"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak,
                          "unit": "TOPS", "frac": achieved / int8_peak, "traffic": traffic,
+                         "traffic_note": ("DRAM bytes of one 4096^3 launch (ncu): the inputs "
+                                          "read once; the 34 MB result drains from L2 after "
+                                          "the launch" if traffic else None),
                          "kernel": "qgemm_tc_kernel (int16d requantization fused"
                                    + (", stores into every rank's output)" if fused else ")"),
                          "peak_note": f"2x {peak_src} bf16 burst {bf16} TFLOP/s"},
