@@ -640,6 +640,32 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
             ml.mode = "parity"
             out[f"wonly_int4d_M{Mx}_fast"] = {"ms": t, "tflops": flops / t / 1e9,
                                               "tensor_frac_bf16": flops / t / 1e9 / bf16}
+    # Decode as a model runs it: one graph of 8 consecutive linears over 8
+    # distinct int4d weights (8 x 24 MB > L2, so no flush is needed and each
+    # weight streams from HBM); time per linear = graph time / 8.  The
+    # single-call lines above also carry the fixed launch and event time.
+    ws8 = []
+    for _ in range(8):
+        lin = torch.nn.Linear(4096, 11008, bias=False, device=dev)
+        with torch.no_grad():
+            lin.weight.normal_(0.0, 0.02)
+        ws8.append(mxb.mx_linear.from_linear(lin, mxb.int4d, 128))
+        del lin
+    for Mx in (1, 16):
+        x = torch.randn(Mx, 4096, generator=g2).bfloat16().to(dev)
+        for m_ in ws8:
+            m_(x)
+
+        def chain(x=x):
+            for m_ in ws8:
+                m_(x)
+        fn = graphed(chain, stream)
+        t = statistics.median(time_steps(fn, steps, lambda: None, stream)) / 8
+        byts = wbytes + x.numel() * 2 + Mx * 11008 * 4
+        out[f"wonly_int4d_M{Mx}_stream8"] = {"ms": t, "gbs": byts / t / 1e6,
+                                             "hbm_frac": byts / t / 1e6 / hbm,
+                                             "note": "per linear in a graph of 8 over distinct weights (192 MB > L2)"}
+    del ws8
     for dt, n in (("int2d", 1 << 28), ("int4d", 1 << 28), ("float4d", 1 << 26)):
         x = torch.randn(n, device=dev)
         d = mxb.get_mx_dtype(dt)

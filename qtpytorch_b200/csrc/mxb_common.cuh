@@ -93,6 +93,38 @@ __device__ __forceinline__ int f4_bucket(float v) {
   return v == v ? i : 15;
 }
 
+// Table form of f4_bucket, for kernels that hold the table in shared memory
+// (80 words, f4_tbl_entry(i) for i < 80).  The boundaries 0 < p0 .. p6 are
+// compared as bit patterns: t = bits(|v|) + (v < 0) turns the negative side's
+// p <= |v| into p < t, as above.  The table has one entry per 1/16 binade
+// (t >> 19) from 2^-5 to 2: the number of boundaries below the cell and the
+// low 19 bits of the boundary inside it (0x7FFFF if none; no cell holds
+// two), so the count is one shared-memory load and one compare instead of
+// the three-step search.  Cells below 2^-5 hold only the boundary 0 (t > 0),
+// cells from 2 up (NaN included) all eight.  Checked equal to f4_bucket for
+// all 2^32 inputs.
+__device__ __forceinline__ uint32_t f4_tbl_entry(int i) {
+  const uint32_t P[8] = {0u, 0x3d2aaaabu, 0x3e000000u, 0x3e555556u,
+                         0x3e955556u, 0x3ed55556u, 0x3f155556u, 0x3f555556u};
+  const uint32_t key = 0x7A0u + (uint32_t)i, start = key << 19;
+  uint32_t c0 = 0, low = 0x7FFFFu;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (P[j] < start) ++c0;
+    else if ((P[j] >> 19) == key) low = P[j] & 0x7FFFFu;
+  }
+  return (c0 << 24) | low;
+}
+
+__device__ __forceinline__ int f4_bucket_tbl(float v, const uint32_t* __restrict__ tbl) {
+  const uint32_t ng = v < 0.0f ? 1u : 0u;  // NaN counts as positive: index 15
+  const uint32_t t = (__float_as_uint(v) & 0x7FFFFFFFu) + ng;
+  const int key = min(max((int)(t >> 19), 0x7A0), 0x7EF) - 0x7A0;
+  const uint32_t e = tbl[key];
+  const int c = (int)(e >> 24) + ((t & 0x7FFFFu) > (e & 0x7FFFFu) ? 1 : 0) - (t == 0u ? 1 : 0);
+  return ng ? 8 - c : 7 + c;
+}
+
 // Sign-extend the low `bits` bits of v.
 __device__ __forceinline__ int sext(uint32_t v, int bits) {
   return (int)(v << (32 - bits)) >> (32 - bits);

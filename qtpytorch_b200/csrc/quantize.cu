@@ -73,10 +73,12 @@ __device__ __forceinline__ uint32_t code_of(float v, float mul) {
 // a block.  Writes the packed codes of these elements at byte offset
 // (e0 * BITS / 8).  With 16 per lane the block's absmax shuffles and scale
 // computation are shared by twice as many elements.
+// f4t: the float4 bucket table in shared memory (f4_bucket_tbl), or nullptr.
 template <int BITS, int MODE, int E = 8>
 __device__ __forceinline__ void quant8_store(const float (&v)[E], bool valid, int L,
                                              int64_t e0, uint8_t* __restrict__ packed,
-                                             float* __restrict__ scales, int64_t blk) {
+                                             float* __restrict__ scales, int64_t blk,
+                                             const uint32_t* f4t = nullptr) {
   float a = 0.0f;
 #pragma unroll
   for (int i = 0; i < E; ++i) a = amax_step(a, v[i]);
@@ -87,7 +89,10 @@ __device__ __forceinline__ void quant8_store(const float (&v)[E], bool valid, in
   if ((threadIdx.x & (L - 1)) == 0) scales[blk] = scale;
   uint32_t cc[E];
 #pragma unroll
-  for (int i = 0; i < E; ++i) cc[i] = code_of<BITS, MODE, MODE == Q_FLOAT4 || BITS == 1>(v[i], mul);
+  for (int i = 0; i < E; ++i)
+    cc[i] = (MODE == Q_FLOAT4 && f4t != nullptr)
+                ? (uint32_t)f4_bucket_tbl(__fdiv_rn(v[i], mul), f4t)
+                : code_of<BITS, MODE, MODE == Q_FLOAT4 || BITS == 1>(v[i], mul);
   if (MODE != Q_FLOAT4 && BITS != 1 && !(mul > 0.0f && mul <= 3.4028235e38f)) {
     // A NaN in the block makes amax and mul NaN, an inf makes the multiplier
     // 0 (the divisor inf): every quotient is then 0 or NaN, and every code 0.
@@ -168,6 +173,13 @@ __global__ void __launch_bounds__(256) quant_vec_kernel(const InT* __restrict__ 
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  __shared__ uint32_t f4s[MODE == Q_FLOAT4 ? 80 : 1];
+  const uint32_t* f4t = nullptr;
+  if constexpr (MODE == Q_FLOAT4) {
+    for (int i = threadIdx.x; i < 80; i += blockDim.x) f4s[i] = f4_tbl_entry(i);
+    __syncthreads();
+    f4t = f4s;
+  }
 #ifndef MXB_Q_BF16_PREFETCH
 #define MXB_Q_BF16_PREFETCH 1
 #endif
@@ -205,7 +217,7 @@ __global__ void __launch_bounds__(256) quant_vec_kernel(const InT* __restrict__ 
                      *reinterpret_cast<float(*)[8]>(v + 8 * h));
       }
       fetch(t + nwarps * 32);
-      quant8_store<BITS, MODE, E>(v, valid, L, t * E, packed, scales, t / L);
+      quant8_store<BITS, MODE, E>(v, valid, L, t * E, packed, scales, t / L, f4t);
     }
   } else {
     for (int64_t w = warp0; w * 32 < groups; w += nwarps) {
@@ -216,7 +228,7 @@ __global__ void __launch_bounds__(256) quant_vec_kernel(const InT* __restrict__ 
       for (int h = 0; h < E / 8; ++h)
         load8<InT>(x, t * E + 8 * h, valid ? n : 0, vec,
                    *reinterpret_cast<float(*)[8]>(v + 8 * h));
-      quant8_store<BITS, MODE, E>(v, valid, L, t * E, packed, scales, t / L);
+      quant8_store<BITS, MODE, E>(v, valid, L, t * E, packed, scales, t / L, f4t);
     }
   }
 }
