@@ -114,16 +114,21 @@ def graphed(fn, stream):
     return g.replay
 
 
-def time_steps(fn, steps, flush, stream=None):
+def time_steps(fn, steps, flush, stream=None, align=None):
     """Device time of each call (CUDA events on the launching stream); L2
     flushed before each timed call.  A short device-side sleep after the flush
     lets the host enqueue the call before the GPU reaches the start event, so
-    the interval holds the call's kernels and not Python launch overhead."""
+    the interval holds the call's kernels and not Python launch overhead.
+    `align` (multi-rank) enqueues a device-side barrier across the ranks
+    before the start event, so every rank's step starts at the same time and
+    no rank's interval holds another rank's host launch delay."""
     st = stream or torch.cuda.current_stream()
     ts = []
     for _ in range(steps):
         flush()
         torch.cuda._sleep(1_000_000)
+        if align is not None:
+            align()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
@@ -291,6 +296,7 @@ def run_ours(args, world, rank, local):
         return sharded_qgemm(qa, w)
 
     stream = torch.cuda.current_stream(dev)
+    align = peers.barrier if fused else None
     # The GEMM kernel alone, for the roofline: at N = 1 the plain matmul
     # (int16d requantization fused); at N > 1 the kernel the step runs, its
     # epilogue storing into every rank's output, without the ordering barrier.
@@ -338,7 +344,7 @@ def run_ours(args, world, rank, local):
     step_g = graphed(step, stream) if (world == 1 or fused) else step
     with Clocks(local) as clk:
         barrier(world)
-        ts = time_steps(step_g, args.steps, flush, stream)
+        ts = time_steps(step_g, args.steps, flush, stream, align)
         barrier(world)
     step_ms = max_over_ranks(sum(ts) / len(ts), world)
     value = 2.0 * M * N * K / (step_ms * 1e-3) / 1e12
@@ -347,7 +353,7 @@ def run_ours(args, world, rank, local):
 
     barrier(world)
     tg = time_steps(graphed(gemm_only, stream) if world == 1 else gemm_only, args.steps, flush,
-                    stream)
+                    stream, align)
     barrier(world)
     gemm_ms = max_over_ranks(sum(tg) / len(tg), world)
     int8_peak = 2.0 * bf16  # kind::i8 issues twice the bf16 rate on sm_100

@@ -264,6 +264,17 @@ int mxb_qgemm_sharded_sync(const void* a_packed, const float* a_scales, int64_t 
                            void* const* sync_blocks, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/*
+ * The cross-rank barrier of mxb_qgemm_sharded_sync on its own: when it has
+ * run on every rank's stream, every rank's earlier work on its stream has
+ * been reached (one-thread kernel, system-scope signals over the same
+ * barrier blocks and call counters, bounded wait of 2 s, then the device
+ * error word holds 6).  Every rank makes the same sequence of barrier and
+ * sharded-matmul calls.  No counterpart in the reference (host plumbing for
+ * the sharded matmul; it lines up the ranks before a timed step).
+ */
+int mxb_peer_barrier(int nranks, int rank, void* const* sync_blocks, void* stream);
+
 /* Map a peer rank's device allocation into this process for the calling
  * thread's current device (cudaIpcOpenMemHandle with lazy peer access):
  * `handle` is the owner's cudaIpcMemHandle_t (handle_bytes == 64); *base

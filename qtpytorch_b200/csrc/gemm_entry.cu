@@ -216,6 +216,17 @@ static int qgemm_sharded_impl(const void* a_packed, const float* a_scales, int64
                   &q, workspace, need, false, static_cast<cudaStream_t>(stream));
 }
 
+int mxb_peer_barrier(int nranks, int rank, void* const* sync_blocks, void* stream) {
+  if (nranks < 1 || nranks > kMaxPeers || rank < 0 || rank >= nranks || !sync_blocks)
+    return MXB_E_ARG;
+  unsigned long long* sync[kMaxPeers] = {};
+  for (int r = 0; r < nranks; ++r) {
+    if (!sync_blocks[r] || ((uintptr_t)sync_blocks[r] & 7)) return MXB_E_ARG;
+    sync[r] = static_cast<unsigned long long*>(sync_blocks[r]);
+  }
+  return peer_barrier(sync, nranks, rank, static_cast<cudaStream_t>(stream));
+}
+
 size_t mxb_linear_wonly_workspace_size(int64_t M, int64_t K, int64_t N, int bits, int kind,
                                        int block, int mode) {
   (void)mode;

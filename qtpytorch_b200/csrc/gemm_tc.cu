@@ -527,6 +527,16 @@ int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int
   return MXB_OK;
 }
 
+int peer_barrier(unsigned long long* const* sync, int nranks, int rank, cudaStream_t st) {
+  QOut q{};
+  q.count = nranks;
+  q.rank = rank;
+  for (int r = 0; r < nranks; ++r) q.sync[r] = sync[r];
+  cross_rank_barrier_kernel<<<1, 32, 0, st>>>(q);
+  MXB_LAUNCH_CHECK();
+  return MXB_OK;
+}
+
 // ── weight-only GEMM (wonly_tc.cuh) ──────────────────────────────────────────
 bool tc_wonly_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w,
                        int64_t N, int bits, int kind, int block, const float* y, bool kmajor) {

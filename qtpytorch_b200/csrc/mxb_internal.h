@@ -59,6 +59,9 @@ struct QOut {
   unsigned long long* sync[kMaxPeers];
   int rank;
 };
+// The cross-rank barrier kernel alone, on stream st (same counters as the
+// barrier that follows a sharded matmul).
+int peer_barrier(unsigned long long* const* sync, int nranks, int rank, cudaStream_t st);
 // Layout of a rank's barrier block (zeroed once by the caller): [1] this
 // rank's call counter, [8 + r] the call counter rank r last signalled to
 // this rank.

@@ -132,6 +132,7 @@ class PeerOutputs:
             self._opened.append(base.value)
             ptr_sync.append(base.value + off)
         self.ptr_sync = (C.c_void_p * world)(*ptr_sync)
+        self._dev = dev
         for _ in range(2):
             words = torch.empty(M * N_full // 2, dtype=torch.int32, device=dev)
             scales = torch.empty(M * N_full // block, dtype=torch.float32, device=dev)
@@ -161,6 +162,18 @@ class PeerOutputs:
                 "words": words, "scales": scales,
                 "ptr_w": (C.c_void_p * world)(*ptr_w), "ptr_s": (C.c_void_p * world)(*ptr_s)})
         self.i = 0
+
+    def barrier(self) -> None:
+        """Device-side barrier over the ranks' barrier blocks on the current
+        stream (mxb_peer_barrier): every rank's earlier work on its stream
+        has been reached when it completes.  Every rank calls it the same
+        number of times, in the same order relative to the fused matmuls."""
+        from . import _lib as L
+        import ctypes as C
+        lib = L.load()
+        st = torch.cuda.current_stream(self._dev).cuda_stream
+        L.check(lib.mxb_peer_barrier(self.world, self.rank, C.cast(self.ptr_sync, C.c_void_p),
+                                     C.c_void_p(st)), "mxb_peer_barrier")
 
     @staticmethod
     def _share(t: torch.Tensor):

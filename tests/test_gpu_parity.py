@@ -167,6 +167,30 @@ def _float4_edge_input():
     return np.stack(rows)
 
 
+@pytest.mark.parametrize("block", [32, 128])
+def test_float4_bucket_table_cells(block):
+    """Blocks with absmax 1 (so the quotient is the value itself): every
+    float within 256 ulp of each 1/16-binade cell edge of the bucket table
+    (2^-6 .. 4) and of each boundary, both signs, plus the zeros: codes
+    equal the oracle's bucketize of the IEEE quotient."""
+    edges = np.arange(0x7A0 - 16, 0x7F0 + 16, dtype=np.int64) << 19
+    bnd = np.abs(O.minifloat4_mids()).view(np.int32).astype(np.int64)
+    centres = np.unique(np.concatenate([edges, bnd]))
+    bits = (centres[:, None] + np.arange(-256, 257, dtype=np.int64)[None, :]).reshape(-1)
+    bits = bits[(bits >= 0) & (bits <= 0x3F800000)]
+    v = bits.astype(np.int32).view(np.float32)
+    v = np.concatenate([v, -v, np.float32([0.0, -0.0])])
+    per = block - 1
+    nb = -(-v.size // per)
+    v = np.concatenate([v, np.zeros(nb * per - v.size, np.float32)]).reshape(nb, per)
+    x = np.concatenate([np.ones((nb, 1), np.float32), v], axis=1).reshape(-1)
+    d = get_mx_dtype("float4d")
+    q = mxb.mx_tensor.quantize(torch.from_numpy(x).cuda(), d, block)
+    p, s, _ = O.quantize(x, d.bits, d.kind, block)
+    assert np.array_equal(q._mx_packed.cpu().numpy(), p)
+    assert np.array_equal(_u32(q._mx_scales.cpu().numpy()), _u32(s))
+
+
 def test_float4_bucket_boundaries():
     x = _float4_edge_input()
     d = get_mx_dtype("float4d")
