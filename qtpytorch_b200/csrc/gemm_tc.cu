@@ -21,6 +21,7 @@
 #include "mxb_internal.h"
 
 #include <cuda.h>
+#include <cstring>
 
 namespace mxb {
 __device__ int g_mxb_device_error = 0;
@@ -45,11 +46,19 @@ constexpr int kTileB = BN * BKB;   // 16 KB
 constexpr int kTmemCols = 2 * BN;  // two int32 accumulators
 constexpr size_t kBarsBytes = 8192;  // >= sizeof(Bars), checked below
 constexpr size_t kSmemBytes = 1024 + (size_t)STAGES * (kTileA + kTileB) + kBarsBytes;
-// int16d codes of a tile staged row by row (BN / 2 words and a 16-byte pad
-// per row, so the lanes' 16-byte writes of 32 consecutive rows hit
-// different bank groups) in the TMA ring, idle once the last MMA is done
-constexpr int kStgRow = BN / 2 + 4;
-static_assert((size_t)BM * kStgRow * 4 <= (size_t)STAGES * kTileA, "staging fits the A ring");
+// int16d codes of a tile staged in the TMA ring (idle once the last MMA is
+// done) as two boxes of 128 rows x 128 bytes (64 codes) in the 128-byte
+// swizzled layout the output tensor maps use (16-byte chunk c of row r at
+// chunk c ^ (r & 7): the lanes' 16-byte writes of consecutive rows hit
+// different bank groups)
+constexpr int kStgBox = BM * 128;
+static_assert(2 * kStgBox <= STAGES * kTileA, "staging fits the A ring");
+
+// Tensor maps of the int16d outputs (codes as 32-bit words, [M][N_full / 2],
+// box 32 words x 128 rows, 128-byte swizzle), one per QOut output.
+struct OutMaps {
+  CUtensorMap m[kMaxPeers];
+};
 
 struct Bars {
   uint64_t full[STAGES];
@@ -109,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const float* __restrict__ sa,
                     const float* __restrict__ sb, int M, int N, int K, float* __restrict__ C,
-                    const __grid_constant__ QOut qout) {
+                    const __grid_constant__ QOut qout, const __grid_constant__ OutMaps omaps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -276,42 +285,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         w[c] = code[0] | (code[1] << 16);
       }
-      // Stage the tile's codes in shared memory, then send whole 256-byte
-      // rows with the bulk copy engine to every buffer of the list: this
-      // rank's output, or, for a column-sharded matmul, the full-width output
-      // of every rank (peer memory over NVLink) at this shard's column
-      // offset.  Whole rows keep NVLink packets full (one lane per row would
-      // send 16-byte pieces of 32 rows per store), and the copies do not hold
-      // the threads on remote latency.
-      uint32_t* stg = reinterpret_cast<uint32_t*>(sA);
+      // Stage the tile's codes in shared memory, then one thread stores both
+      // boxes with TMA tile stores into every output of the list: this
+      // rank's, or, for a column-sharded matmul, the full-width output of
+      // every rank (peer memory over NVLink) at this shard's column offset.
+      // Two 16 KB stores per output keep NVLink packets full and leave the
+      // threads free; the CTA waits only until the staging has been read.
+      uint8_t* stg = sA + (col0 >> 6) * kStgBox + row * 128;
+      const int ch0 = (col0 & 63) >> 3;  // first 16-byte chunk of this warp's columns
 #pragma unroll
       for (int c = 0; c < kEpiCols / 8; ++c)
-        *reinterpret_cast<uint4*>(stg + row * kStgRow + col0 / 2 + 4 * c) =
+        *reinterpret_cast<uint4*>(stg + (((ch0 + c) ^ (row & 7)) << 4)) =
             make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
       if (ew < 4) bars->row_scale[row] = cs;
       fence_proxy_async_shared();
       asm volatile("bar.sync 2, %0;" ::"n"(kEpiWarps * 32) : "memory");
       const int te = threadIdx.x - 64;  // 0 .. 511
-      constexpr int kRowsPerLane = BM / (kEpiWarps * 2);  // 2 issuing lanes per warp
-      if (lane < 2) {
-        const int r0 = (ew * 2 + lane) * kRowsPerLane;
-        for (int r = 0; r < qout.count; ++r)
-          for (int rr = r0; rr < r0 + kRowsPerLane; ++rr) {
-            const size_t e = (size_t)(m0 + rr) * qout.row_stride + qout.col_off + n0;
-            bulk_store_s2g(qout.words[r] + e / 2, stg + rr * kStgRow, BN * 2);
-          }
+      if (te == 0) {
+        const int x0 = (qout.col_off + n0) >> 1;  // in 32-bit words: a multiple of 64
+        for (int r = 0; r < qout.count; ++r) {
+          tma_store_2d(&omaps.m[r], sA, x0, m0);
+          tma_store_2d(&omaps.m[r], sA + kStgBox, x0 + 32, m0);
+        }
         bulk_commit();
       }
       if (te < BM) {
         const size_t e = (size_t)(m0 + te) * qout.row_stride + qout.col_off + n0;
         for (int r = 0; r < qout.count; ++r) qout.scales[r][e / BN] = bars->row_scale[te];
       }
-      // The CTA waits only for its staging buffer to be read; the row copies
-      // (over NVLink for peers) finish while the next tiles compute, and are
-      // complete when the kernel is, which the post-launch barrier (the
-      // cross-rank barrier kernel, or a collective) orders before any rank
-      // reads.
-      if (lane < 2) bulk_wait_read();
+      // The row copies (over NVLink for peers) finish while the next tiles
+      // compute, and are complete when the kernel is, which the post-launch
+      // barrier (the cross-rank barrier kernel, or a collective) orders
+      // before any rank reads.
+      if (te == 0) bulk_wait_read();
     }
   }
   __syncthreads();
@@ -517,8 +523,17 @@ int tc_qgemm(const void* a, const float* sa, const void* b, const float* sb, int
                                     (int)kSmemBytes));
   dim3 grid((unsigned)(N / BN), (unsigned)(M / BM));
   QOut none{};
+  OutMaps om;
+  memset(&om, 0, sizeof(om));
+  if (qout) {
+    for (int r = 0; r < qout->count; ++r)
+      if (make_tmap_2d(&om.m[r], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, qout->words[r],
+                       (uint64_t)qout->row_stride / 2, (uint64_t)M, 32, BM,
+                       CU_TENSOR_MAP_SWIZZLE_128B) != MXB_OK)
+        return MXB_E_CUDA;
+  }
   kern<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, sa, sb, (int)M, (int)N, (int)K, C,
-                                           qout ? *qout : none);
+                                           qout ? *qout : none, om);
   MXB_LAUNCH_CHECK();
   if (qout && qout->sync[0] != nullptr) {
     cross_rank_barrier_kernel<<<1, 32, 0, st>>>(*qout);

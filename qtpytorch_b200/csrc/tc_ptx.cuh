@@ -115,6 +115,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 2-D tiled TMA store shared -> global (bulk group completion; x, y >= 0).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x,
+                                             int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
 // Bulk copy shared -> global (no tensor map, no multicast): both addresses
 // 16-byte aligned, bytes a multiple of 16; completes in the issuing
 // thread's bulk group.
