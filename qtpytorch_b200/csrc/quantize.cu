@@ -1066,7 +1066,10 @@ int quant_flat(const InT* x, int64_t n, int block, uint8_t* packed, float* scale
     // 16 elements per lane where the block allows: the per-block shuffles
     // and scale arithmetic are shared by twice the elements (measured at 2^26
     // elements: int4d 0.77 -> 0.85 of HBM from fp32, 0.43 -> 0.56 from bf16)
-    if (block % 16 == 0)
+    if (sizeof(InT) == 2 && block % 32 == 0)
+      quant_vec_kernel<InT, BITS, MODE, 32><<<grid_for(nb * (block / 32)), 256, 0, st>>>(
+          x, n, block, nb, vec, packed, scales);
+    else if (block % 16 == 0)
       quant_vec_kernel<InT, BITS, MODE, 16><<<grid_for(nb * (block / 16)), 256, 0, st>>>(
           x, n, block, nb, vec, packed, scales);
     else
