@@ -870,6 +870,49 @@ __global__ void __launch_bounds__(256) hquant_fast_kernel(
   }
 }
 
+// Final stage of the row kernels: out[i] = div(v, sqrt n) (times signs[i]
+// when `sgn`), in runs of kG consecutive elements as 16-byte loads and
+// stores where the row allows (phase C layout, d % kG == 0, 16-byte aligned
+// row), one element at a time otherwise.
+template <class W>
+__device__ __forceinline__ void store_row(const float (&v)[W::kN / 256], float* __restrict__ orow,
+                                          int d, float sqrtn, float rsq, int dmode,
+                                          const float* __restrict__ signs, bool sgn) {
+  constexpr int V = W::kN / 256;
+  const int t = threadIdx.x;
+  if (W::kPhaseC && d % W::kG == 0 && ((uintptr_t)orow & 15) == 0) {
+#pragma unroll
+    for (int q = 0; q < W::kRuns; ++q) {
+      const int i0 = W::idx(t, q * W::kG);
+      if (i0 >= d) continue;
+#pragma unroll
+      for (int c4 = 0; c4 < W::kG / 4; ++c4) {
+        const float* vv = v + q * W::kG + 4 * c4;
+        float4 o = make_float4(whtr::div_sqrtn(vv[0], sqrtn, rsq, dmode),
+                               whtr::div_sqrtn(vv[1], sqrtn, rsq, dmode),
+                               whtr::div_sqrtn(vv[2], sqrtn, rsq, dmode),
+                               whtr::div_sqrtn(vv[3], sqrtn, rsq, dmode));
+        if (sgn) {
+          const float4 sg = __ldg(reinterpret_cast<const float4*>(signs + i0) + c4);
+          o = make_float4(__fmul_rn(o.x, sg.x), __fmul_rn(o.y, sg.y), __fmul_rn(o.z, sg.z),
+                          __fmul_rn(o.w, sg.w));
+        }
+        reinterpret_cast<float4*>(orow + i0)[c4] = o;
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int i = W::idx(t, j);
+    if (i < d) {
+      float o = whtr::div_sqrtn(v[j], sqrtn, rsq, dmode);
+      if (sgn) o = __fmul_rn(o, __ldg(signs + i));
+      orow[i] = o;
+    }
+  }
+}
+
 template <int BITS, int KIND, int V>
 __global__ void __launch_bounds__(256) hdequant_fast_kernel(
     const uint8_t* __restrict__ packed, const float* __restrict__ scales, int d, float sqrtn,
@@ -910,12 +953,20 @@ __global__ void __launch_bounds__(256) hdequant_fast_kernel(
           word = __ldg(p);
         }
       }
+      // a run lies inside one scale block when blocks are whole runs and
+      // the row starts on a run boundary of its blocks: one scale load
+      const bool run_blk = block % W::kG == 0 && off % W::kG == 0;
+      const int k0 = off + i0;
+      const float sc0 = (run_blk && i0 < d)
+                            ? __ldg(srow_s + (bshift >= 0 ? (k0 >> bshift) : k0 / block))
+                            : 0.0f;
 #pragma unroll
       for (int c = 0; c < W::kG; ++c) {
         float a = 0.0f;
         if (i0 < d) {
           const int k = off + i0 + c;
-          const float sc = __ldg(srow_s + (bshift >= 0 ? (k >> bshift) : k / block));
+          const float sc =
+              run_blk ? sc0 : __ldg(srow_s + (bshift >= 0 ? (k >> bshift) : k / block));
           uint32_t raw;
           if constexpr (RB == 16) {
             raw = c < 8 ? (uint32_t)(word >> (8 * c)) & 0xffu
@@ -943,11 +994,7 @@ __global__ void __launch_bounds__(256) hdequant_fast_kernel(
     }
   }
   W::transform(v, srow);
-#pragma unroll
-  for (int j = 0; j < V; ++j) {
-    const int i = W::idx(t, j);
-    if (i < d) out[e0 + i] = __fmul_rn(whtr::div_sqrtn(v[j], sqrtn, rsq, dmode), __ldg(signs + i));
-  }
+  store_row<W>(v, out + e0, d, sqrtn, rsq, dmode, signs, true);
 }
 
 template <int V>
@@ -995,15 +1042,7 @@ __global__ void __launch_bounds__(256) hrows_fast_kernel(const float* __restrict
     }
   }
   W::transform(v, srow);  // ends with __syncthreads: in-place x == out is safe
-#pragma unroll
-  for (int j = 0; j < V; ++j) {
-    const int i = W::idx(t, j);
-    if (i < d) {
-      float o = whtr::div_sqrtn(v[j], sqrtn, rsq, dmode);
-      if (inverse) o = __fmul_rn(o, __ldg(signs + i));
-      out[r * d + i] = o;
-    }
-  }
+  store_row<W>(v, out + r * d, d, sqrtn, rsq, dmode, signs, inverse);
 }
 
 // ── host side ────────────────────────────────────────────────────────────────
