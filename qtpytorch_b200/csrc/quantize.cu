@@ -998,7 +998,7 @@ __global__ void __launch_bounds__(256) hdequant_fast_kernel(
 }
 
 template <int V>
-__global__ void __launch_bounds__(256) hrows_fast_kernel(const float* __restrict__ x, int d,
+__global__ void __launch_bounds__(256, V <= 32 ? 4 : 1) hrows_fast_kernel(const float* __restrict__ x, int d,
                                                          float sqrtn, float rsq, int dmode,
                                                          const float* __restrict__ signs,
                                                          bool inverse, float* __restrict__ out) {
@@ -1158,6 +1158,8 @@ int quant_dispatch(const InT* x, int64_t n, int64_t row_len, int variant, int bl
     auto launch_fast = [&](auto kf, int V) -> int {
       const size_t fs = ((size_t)hn + (size_t)(hn / 256) * (256 / V)) * sizeof(float);
       MXB_CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fs));
+      MXB_CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        (int)cudaSharedmemCarveoutMaxShared));
       kf<<<(unsigned)rows, 256, fs, st>>>(x, (int)d, sqrtn, 1.0f / sqrtn, div_mode(hn), signs,
                                           block, fuse, packed, scales, rot);
       MXB_LAUNCH_CHECK();
@@ -1487,6 +1489,8 @@ int mxb_hadamard_rows(const float* x, int64_t rows, int64_t d, const float* sign
     auto launch_fast = [&](auto kf, int V) -> int {
       const size_t fs = ((size_t)hn + (size_t)(hn / 256) * (256 / V)) * sizeof(float);
       MXB_CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fs));
+      MXB_CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        (int)cudaSharedmemCarveoutMaxShared));
       kf<<<(unsigned)rows, 256, fs, st>>>(x, (int)d, sqrtn, 1.0f / sqrtn, div_mode(hn), signs,
                                           inverse != 0, out);
       MXB_LAUNCH_CHECK();
