@@ -689,6 +689,16 @@ int tc_wonly_dec(const void* x, int64_t M, int64_t K, const void* w, const float
 
 }  // namespace mxb
 
+namespace mxb {
+// Device address of the error word for kernels of other translation units
+// (looked up with the device current; nullptr if that fails).
+int* device_error_ptr() {
+  void* p = nullptr;
+  return cudaGetSymbolAddress(&p, g_mxb_device_error) == cudaSuccess ? static_cast<int*>(p)
+                                                                    : nullptr;
+}
+}  // namespace mxb
+
 extern "C" int mxb_device_error(int clear) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, mxb::g_mxb_device_error, sizeof(int)) != cudaSuccess)

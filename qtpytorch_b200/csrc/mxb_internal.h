@@ -59,6 +59,9 @@ struct QOut {
   unsigned long long* sync[kMaxPeers];
   int rank;
 };
+// Device address of the library's device error word (mxb_device_error), for
+// kernels outside gemm_tc.cu; nullptr if the lookup fails.
+int* device_error_ptr();
 // The cross-rank barrier kernel alone, on stream st (same counters as the
 // barrier that follows a sharded matmul).
 int peer_barrier(unsigned long long* const* sync, int nranks, int rank, cudaStream_t st);

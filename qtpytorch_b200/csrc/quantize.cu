@@ -10,6 +10,7 @@
 // true division for float4 and for the matmul requantization, round half to
 // even.  Built without fast-math so every `__f*_rn` is one IEEE rounding.
 #include "mxb_common.cuh"
+#include "mxb_internal.h"
 #include "wht_regs.cuh"
 
 #include <math.h>
@@ -1045,6 +1046,106 @@ __global__ void __launch_bounds__(256, V <= 32 ? 4 : 1) hrows_fast_kernel(const 
   store_row<W>(v, out + r * d, d, sqrtn, rsq, dmode, signs, inverse);
 }
 
+// ── pipelined row transform ──────────────────────────────────────────────────
+// Persistent CTAs (a few per SM) walk rows r, r + grid, ...; one thread
+// requests the next row as a single bulk copy (cp.async.bulk global ->
+// shared, completion on an mbarrier, no multicast) while the CTA transforms
+// the current one, so each row's DRAM latency is hidden behind the previous
+// row's work.  The row buffer doubles as the transform's scratch once its
+// values are in registers.  Waits are bounded (2 s of %globaltimer); on
+// expiry the kernel records code 7 in the library's error word, waits
+// (bounded) for its other copy in flight and returns.
+constexpr int kErrRowLoad = 7;  // error-word code of a row copy that never landed
+
+__device__ __forceinline__ uint32_t sm_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void row_bar_init(uint64_t* b) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_addr(b)));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void row_copy(float* dst, const float* src, uint32_t bytes,
+                                         uint64_t* b) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+          sm_addr(b)),
+      "r"(bytes)
+      : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          sm_addr(dst)),
+      "l"(src), "r"(bytes), "r"(sm_addr(b))
+      : "memory");
+}
+__device__ __forceinline__ bool row_wait(uint64_t* b, uint32_t parity) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(sm_addr(b)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 15) == 15) {
+      uint64_t t1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+      if (t1 - t0 > 2000000000ull) break;
+    }
+  }
+  return false;
+}
+
+template <int V>
+__global__ void __launch_bounds__(256, 3) hrows_pipe_kernel(const float* __restrict__ x,
+                                                           int64_t rows, int d, float sqrtn,
+                                                           float rsq, int dmode,
+                                                           const float* __restrict__ signs,
+                                                           bool inverse, float* __restrict__ out,
+                                                           int* __restrict__ err) {
+  using W = whtr::Row<V>;
+  static_assert(W::kPhaseC, "runs layout");
+  extern __shared__ __align__(128) float sm[];
+  __shared__ __align__(8) uint64_t bar[2];
+  const int t = threadIdx.x;
+  const uint32_t bytes = (uint32_t)d * 4u;
+  if (t == 0) {
+    row_bar_init(&bar[0]);
+    row_bar_init(&bar[1]);
+  }
+  __syncthreads();
+  int64_t r = blockIdx.x;
+  if (t == 0 && r < rows) row_copy(sm, x + r * d, bytes, &bar[0]);
+  for (int i = 0; r < rows; ++i, r += gridDim.x) {
+    const int cur = i & 1;
+    const int64_t rn = r + gridDim.x;
+    // `next` was the previous row's scratch, released by the transform's
+    // closing barrier
+    float* const mine = sm + cur * W::kSmemFloats;
+    float* const next = sm + (cur ^ 1) * W::kSmemFloats;
+    if (t == 0 && rn < rows) row_copy(next, x + rn * d, bytes, &bar[cur ^ 1]);
+    const bool ok = __syncthreads_and(row_wait(&bar[cur], (i >> 1) & 1));
+    if (!ok) {
+      if (t == 0) {
+        if (err) atomicCAS(err, 0, kErrRowLoad);
+        if (rn < rows) row_wait(&bar[cur ^ 1], ((i + 1) >> 1) & 1);
+      }
+      return;
+    }
+    float v[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int k = W::idxA(t, j);
+      v[j] = inverse ? mine[k] : __fmul_rn(mine[k], __ldg(signs + k));
+    }
+    W::transform(v, mine);  // opens and closes with __syncthreads
+    store_row<W>(v, out + r * d, d, sqrtn, rsq, dmode, signs, inverse);
+  }
+}
+
 // ── host side ────────────────────────────────────────────────────────────────
 constexpr int kMaxHadamardN = 32768;
 
@@ -1485,6 +1586,24 @@ int mxb_hadamard_rows(const float* x, int64_t rows, int64_t d, const float* sign
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const float sqrtn = (float)sqrt((double)hn);
   const int fv = wht_fast_v(hn);
+  // pipelined kernel: whole power-of-two rows, 16-byte aligned, enough rows
+  // to keep every CTA busy for a few rows
+  if ((fv == 16 || fv == 32) && d == hn && ((uintptr_t)x & 15) == 0 &&
+      ((uintptr_t)out & 15) == 0 && rows >= 4 * kSMs) {
+    auto kp = fv == 16 ? hrows_pipe_kernel<16> : hrows_pipe_kernel<32>;
+    const size_t fs = 2 * ((size_t)hn + (size_t)(hn / 256) * (256 / fv)) * sizeof(float);
+    MXB_CUDA_TRY(cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fs));
+    MXB_CUDA_TRY(cudaFuncSetAttribute(kp, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      (int)cudaSharedmemCarveoutMaxShared));
+    int per_sm = 0;
+    MXB_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kp, 256, fs));
+    if (per_sm < 1) per_sm = 1;
+    const int64_t grid = rows < (int64_t)per_sm * kSMs ? rows : (int64_t)per_sm * kSMs;
+    kp<<<(unsigned)grid, 256, fs, st>>>(x, rows, (int)d, sqrtn, 1.0f / sqrtn, div_mode(hn), signs,
+                                        inverse != 0, out, device_error_ptr());
+    MXB_LAUNCH_CHECK();
+    return MXB_OK;
+  }
   if (fv) {
     auto launch_fast = [&](auto kf, int V) -> int {
       const size_t fs = ((size_t)hn + (size_t)(hn / 256) * (256 / V)) * sizeof(float);

@@ -25,6 +25,7 @@ enum DeviceError : int {
   kErrTimeoutTmemEmpty = 4,
   kErrTimeoutDone = 5,
   kErrTimeoutPeer = 6,  // a peer rank never signalled the cross-rank barrier
+  kErrTimeoutRowLoad = 7,  // a row's bulk copy into shared memory never completed (row transforms)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -404,6 +404,25 @@ def test_decode_gemv_shapes(M, dt, K, N, block, x_dt):
         _linear_check(y.cpu().numpy(), x.float().numpy(), wdq)
 
 
+@pytest.mark.parametrize("d,rows", [(4096, 700), (8192, 600), (8192, 1777)])
+def test_pipelined_wht_rows_bit_exact(d, rows):
+    """Enough whole power-of-two rows for the pipelined row kernel (each
+    persistent CTA copies its next row into shared memory while it
+    transforms the current one), row counts that leave CTAs with different
+    numbers of rows: rotation and unrotation bit-identical to the oracle,
+    and no device error recorded."""
+    seed = get_mx_dtype("int4dh").hadamard_seed
+    g = torch.Generator().manual_seed(rows)
+    x = torch.randn(rows, d, generator=g)
+    signs = mxb.sign_vector(d, seed).numpy()
+    L.load().mxb_device_error(1)
+    rot = ops.hadamard_rows(x.cuda(), seed, inverse=False).cpu().numpy()
+    assert np.array_equal(_u32(rot), _u32(O.rotate(x.numpy(), signs)))
+    un = ops.hadamard_rows(x.cuda(), seed, inverse=True).cpu().numpy()
+    assert np.array_equal(_u32(un), _u32(O.unrotate(x.numpy(), signs)))
+    assert L.load().mxb_device_error(1) == 0
+
+
 @pytest.mark.parametrize("d,dtn", [(2048, "int4dh"), (3000, "int4dh"), (4096, "int4dh"),
                                    (8192, "int4dh"), (12000, "int4dh"), (16384, "int4dh"),
                                    (4096, "int8dh"), (8192, "int8dh"), (8192, "int2dh"),
