@@ -423,6 +423,25 @@ def test_pipelined_wht_rows_bit_exact(d, rows):
     assert L.load().mxb_device_error(1) == 0
 
 
+@pytest.mark.parametrize("dtn,block", [("int4dh", 128), ("int2dh", 32), ("float4dh", 128),
+                                       ("int8dh", 64), ("int1dh", 128)])
+def test_h_quantize_many_rows_bit_exact(dtn, block):
+    """fp32 h quantize of 640 rows of 8192 with an outlier channel (the
+    register-WHT kernel over many CTAs): packed codes and scales
+    bit-identical to the oracle."""
+    dt = get_mx_dtype(dtn)
+    g = torch.Generator().manual_seed(block)
+    x = torch.randn(640, 8192, generator=g)
+    x[:, 17] *= 25.0  # an outlier channel
+    signs = mxb.sign_vector(8192, dt.hadamard_seed).numpy()
+    L.load().mxb_device_error(1)
+    q = mxb.mx_tensor.quantize(x.cuda(), dt, block)
+    p, s, _ = O.quantize(x.numpy(), dt.bits, dt.kind, block, True, signs)
+    assert np.array_equal(q._mx_packed.cpu().numpy(), p)
+    assert np.array_equal(_u32(q._mx_scales.cpu().numpy()), _u32(s))
+    assert L.load().mxb_device_error(1) == 0
+
+
 @pytest.mark.parametrize("d,dtn", [(2048, "int4dh"), (3000, "int4dh"), (4096, "int4dh"),
                                    (8192, "int4dh"), (12000, "int4dh"), (16384, "int4dh"),
                                    (4096, "int8dh"), (8192, "int8dh"), (8192, "int2dh"),
