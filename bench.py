@@ -246,7 +246,8 @@ def run_ours(args, world, rank, local):
     def flush():
         flush_buf.zero_()
 
-    if args.only in ("gemv1", "gemv16", "wo2048", "quant", "dequant", "h"):
+    if args.only in ("gemv1", "gemv16", "wo2048", "wo2048_fast", "quant", "quant_f4", "dequant",
+                     "h"):
         print(json.dumps(run_extras(args, dev, flush, torch.cuda.current_stream(dev), hbm, bf16)))
         return
     if args.only == "sweep":  # the full configs[4] sweep (a few minutes), one JSON line
@@ -589,12 +590,13 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
     from qtpytorch_b200 import ops
     out = {}
     steps = max(3, min(args.steps, 10))
-    if args.only == "quant":  # profiling case: int4d quantize of 2^26 fp32 values
-        x = torch.randn(1 << 26, device=dev)
+    if args.only in ("quant", "quant_f4"):  # profiling case: int4d (float4d) quantize of
+        x = torch.randn(1 << 26, device=dev)  # 2^26 fp32 values
+        dt = mxb.int4d if args.only == "quant" else mxb.get_mx_dtype("float4d")
         for _ in range(3 + args.steps):
-            ops.quantize(x, mxb.int4d, 128)
+            ops.quantize(x, dt, 128)
         torch.cuda.synchronize()
-        return {"only": "quant"}
+        return {"only": args.only}
     if args.only == "h":  # profiling case: int4dh quantize / dequantize of W^T 8192 x 8192
         # and the row unrotation of y 4096 x 8192
         dt = mxb.get_mx_dtype("int4dh")
@@ -621,7 +623,10 @@ def run_extras(args, dev, flush, stream, hbm, bf16):
     ml = mxb.mx_linear.from_linear(lin.to(dev), mxb.int4d, 128)
     wbytes = ml._mx_weight._mx_packed.numel() + ml._mx_weight._mx_scales.numel() * 4
     g2 = torch.Generator().manual_seed(2)
-    only = {"gemv1": (1,), "gemv16": (16,), "wo2048": (2048,)}.get(args.only)
+    only = {"gemv1": (1,), "gemv16": (16,), "wo2048": (2048,), "wo2048_fast": (2048,)}.get(
+        args.only)
+    if args.only == "wo2048_fast":
+        ml.mode = "fast"
     for Mx in only or (1, 16, 128, 2048):
         x = torch.randn(Mx, 4096, generator=g2).bfloat16().to(dev)
         for _ in range(3):
@@ -790,7 +795,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
                     help="N > 1: output gather fused into the GEMM kernel, or NCCL all-gather")
-    ap.add_argument("--only", default=None, choices=["gemm", "gemm8192", "gemv1", "gemv16", "wo2048", "quant", "dequant", "h",
+    ap.add_argument("--only", default=None, choices=["gemm", "gemm8192", "gemv1", "gemv16", "wo2048", "wo2048_fast", "quant",
+                             "quant_f4", "dequant", "h",
                              "sweep"],
                     help="run one kernel case untimed (for profiling)")
     args = ap.parse_args()
