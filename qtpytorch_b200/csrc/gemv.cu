@@ -116,6 +116,9 @@ __global__ void __launch_bounds__(kWideWarps * 32) gemv_wide_kernel(
     const float* __restrict__ ws, int N, int block, int krows, float* __restrict__ part) {
   constexpr int CPT = LB * 8 / BITS;
   constexpr int kCols = 32 * CPT;  // columns of one CTA
+  // the split-reduce kernel that follows may be scheduled now (it waits
+  // for this grid's completion before reading the partial sums)
+  asm volatile("griddepcontrol.launch_dependents;");
   extern __shared__ __align__(16) float sm[];
   float* xs = sm;                    // [MT][krows]
   float* red = sm + MT * krows;      // [kWideWarps][MT][kCols]
@@ -207,9 +210,13 @@ __global__ void __launch_bounds__(kWideWarps * 32) gemv_wide_kernel(
   }
 }
 
+// Launched as a programmatic dependent of the split kernel (it may start
+// while that kernel drains); griddepcontrol.wait returns once the split
+// kernel has completed and its partial sums are visible.
 __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ part,
                                                            int splits, int64_t mn,
                                                            float* __restrict__ y) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn;
        i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.0f;
@@ -393,7 +400,17 @@ int gemv_run(const GemvPlan& plan, const void* x, int x_dtype, int64_t M, int64_
   const int64_t mn = M * N;
   int64_t g = cdiv(mn, 256);
   if (g > kSMs * 8) g = kSMs * 8;
-  split_reduce_kernel<<<(unsigned)g, 256, 0, st>>>(partial, plan.splits, mn, y);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)g);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MXB_CUDA_TRY(cudaLaunchKernelEx(&cfg, split_reduce_kernel, (const float*)partial, plan.splits,
+                                  mn, y));
   MXB_LAUNCH_CHECK();
   return MXB_OK;
 }
