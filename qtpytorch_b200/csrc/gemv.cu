@@ -307,7 +307,7 @@ GemvPlan gemv_plan(int64_t M, int64_t K, int64_t N, int bits, int kind, int bloc
   if (M >= 1 && K >= 1 && ((uintptr_t)y % 16) == 0 &&
       tc_dec_eligible(x, x_dtype, M, K, w, N, bits, kind, block)) {
     int splits, kc;
-    tc_dec_plan(K, N, &splits, &kc);
+    tc_dec_plan(M, K, N, &splits, &kc);
     p.ok = true;
     p.kernel = 4;
     p.splits = splits;

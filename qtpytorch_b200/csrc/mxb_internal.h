@@ -91,7 +91,7 @@ int tc_wonly(const void* x, int64_t M, int64_t K, const void* w, const float* ws
              bool kmajor = false);
 bool tc_dec_eligible(const void* x, int x_dtype, int64_t M, int64_t K, const void* w, int64_t N,
                      int bits, int kind, int block);
-void tc_dec_plan(int64_t K, int64_t N, int* splits, int* kc);
+void tc_dec_plan(int64_t M, int64_t K, int64_t N, int* splits, int* kc);
 int tc_wonly_dec(const void* x, int64_t M, int64_t K, const void* w, const float* ws, int64_t N,
                  int bits, int block, int kc, int splits, float* out, cudaStream_t st);
 }  // namespace mxb
