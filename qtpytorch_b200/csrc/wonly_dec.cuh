@@ -81,16 +81,20 @@ template <int BITS>
 __device__ __forceinline__ uint4 codes8_bf16(const uint8_t* p) {
   uint32_t o[4];
   if constexpr (BITS == 4) {
-    // offset binary u = code + 8 under exponent byte 0x4B reads as 2^23 + u
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(p) ^ 0x88888888u;
-    const uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
-    const uint64_t bias = pack2(8388616.0f, 8388616.0f);  // 2^23 + 8
+    // offset binary u = code + 8 placed in the mantissa of bf16 128 (0x4300)
+    // reads as 128 + u; one packed bf16 subtraction of 136 leaves the code
+    // (exact: small integers).  Byte k of t holds codes 2k (low nibble) and,
+    // shifted down in s, 2k + 1.
+    const uint32_t t = *reinterpret_cast<const uint32_t*>(p) ^ 0x88888888u;
+    const uint32_t s = t >> 4;
+    const __nv_bfloat162 bias = __floats2bfloat162_rn(136.0f, 136.0f);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float2 c = unpack2(fsub2(pack2(__int_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + k)),
-                                           __int_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + k))),
-                                     bias));
-      o[k] = hi_halves(c.x, c.y);
+      // result byte 0 = byte k of t, byte 2 = byte k of s (bytes 1, 3 masked)
+      const uint32_t sel = (uint32_t)(k | (k << 4) | ((4 + k) << 8) | ((4 + k) << 12));
+      const uint32_t x = (__byte_perm(t, s, sel) & 0x000F000Fu) | 0x43004300u;
+      __nv_bfloat162 c = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&x), bias);
+      o[k] = *reinterpret_cast<uint32_t*>(&c);
     }
   } else if constexpr (BITS == 8) {
     const uint2 w = *reinterpret_cast<const uint2*>(p);
