@@ -236,7 +236,7 @@ def run_ours(args, world, rank, local):
     from qtpytorch_b200 import _lib as L
     from qtpytorch_b200 import ops
     from qtpytorch_b200.parallel import (PeerOutputs, ShardedQGemmWeight, sharded_qgemm,
-                                         sharded_qgemm_fused)
+                                         sharded_qgemm_fused, sharded_qgemm_pull)
 
     dev = torch.device("cuda", local)
     lib = L.load()
@@ -273,7 +273,10 @@ def run_ours(args, world, rank, local):
     # N > 1: each rank's GEMM epilogue writes its int16d tiles into every
     # rank's full output over NVLink (CUDA IPC peer mappings), then one
     # one-element all-reduce orders the ranks; no gather or reorder pass
-    fused = world > 1 and args.gather == "fused"
+    # "pull": each rank's GEMM writes only its own output, the ranks' SMs
+    # then read the peers' shards (same peer mappings, same barrier kernel)
+    fused = world > 1 and args.gather in ("fused", "pull")
+    pull = fused and args.gather == "pull"
     peers, fuse_note = None, None
     if fused:
         # all ranks map their peers' outputs; if any rank cannot, all use
@@ -292,6 +295,8 @@ def run_ours(args, world, rank, local):
             fuse_note = fuse_note or "a peer rank could not map the outputs"
 
     def step():
+        if pull:
+            return sharded_qgemm_pull(qa, w, peers)
         if fused:
             return sharded_qgemm_fused(qa, w, peers)
         return sharded_qgemm(qa, w)
@@ -312,9 +317,12 @@ def run_ours(args, world, rank, local):
             out = peers.next()
             rc = lib.mxb_qgemm_sharded(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales),
                                        qa._mx_scales.numel(), L.ptr(w.codes), L.ptr(w.scales),
-                                       w.scales.numel(), M, K, nl, 8, BLOCK, N, w.n0, world,
-                                       C.cast(out["ptr_w"], C.c_void_p),
-                                       C.cast(out["ptr_s"], C.c_void_p), L.ptr(ws), wsb,
+                                       w.scales.numel(), M, K, nl, 8, BLOCK, N, w.n0,
+                                       1 if pull else world,
+                                       C.cast((C.c_void_p * 1)(out["ptr_w"][rank]) if pull
+                                              else out["ptr_w"], C.c_void_p),
+                                       C.cast((C.c_void_p * 1)(out["ptr_s"][rank]) if pull
+                                              else out["ptr_s"], C.c_void_p), L.ptr(ws), wsb,
                                        torch.cuda.current_stream(dev).cuda_stream)
             L.check(rc, "mxb_qgemm_sharded")
             return
@@ -369,7 +377,7 @@ def run_ours(args, world, rank, local):
     # A's codes and every rank's B block scales (the reference's B-scale view
     # pairs a column with other rows' blocks), runs the sharded matmul and
     # reads back its rows of the replicated result.
-    e2e_step, h2d, d2h = make_e2e_step(a_h, b_h, w, peers, fused, world, rank, dev)
+    e2e_step, h2d, d2h = make_e2e_step(a_h, b_h, w, peers, fused, world, rank, dev, pull)
     for _ in range(2):
         e2e_step()
     barrier(world)
@@ -408,8 +416,10 @@ def run_ours(args, world, rank, local):
                                    "(configs[1])",
                        "global_batch": M,
                        "parallelism": f"N-sharded x{world}" + (
-                           ", output gather fused into the GEMM epilogue (peer stores, "
-                           "completion barrier kernel over peer flags)"
+                           (", local GEMM, barrier kernel over peer flags, then every SM "
+                            "pulls the peers' shards over NVLink" if pull else
+                            ", output gather fused into the GEMM epilogue (peer stores, "
+                            "completion barrier kernel over peer flags)")
                            if fused else (", NCCL all-gather" if world > 1 else "")
                            + (f" ({fuse_note})" if fuse_note else "")),
                        "l2": "flushed (256 MiB write) before every timed step"},
@@ -419,7 +429,8 @@ def run_ours(args, world, rank, local):
                                           "read once; the 34 MB result drains from L2 after "
                                           "the launch" if traffic else None),
                          "kernel": "qgemm_tc_kernel (int16d requantization fused"
-                                   + (", stores into every rank's output)" if fused else ")"),
+                                   + (", stores into every rank's output)" if fused and not pull
+                                      else ")"),
                          "peak_note": f"2x {peak_src} bf16 burst {bf16} TFLOP/s"},
             "cpu_baseline": cpu,
             "e2e": {"value": 2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
@@ -428,7 +439,7 @@ def run_ours(args, world, rank, local):
             "gemm_ms": gemm_ms,
             "nvlink": ({"peer_bytes_per_launch": peer_bytes,
                         "gbs_per_direction": peer_bytes / (gemm_ms * 1e-3) / 1e9,
-                        "link_ref_gbs": 770.0} if fused else None),
+                        "link_ref_gbs": 770.0} if fused and not pull else None),
             "config3_sharded": sharded3,
             "check": check,
             "gpu_launches": int(launches),
@@ -438,12 +449,12 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-def make_e2e_step(a_h, b_h, w, peers, fused, world, rank, dev):
+def make_e2e_step(a_h, b_h, w, peers, fused, world, rank, dev, pull=False):
     """One call of the user-facing path from host buffers (see run_ours)."""
     import qtpytorch_b200 as mxb
     from qtpytorch_b200 import ops
     from qtpytorch_b200.parallel import (ShardedQGemmWeight, row_shard, sharded_qgemm,
-                                         sharded_qgemm_fused)
+                                         sharded_qgemm_fused, sharded_qgemm_pull)
     r0, r1 = [b * BLOCK // K for b in row_shard(M * K // BLOCK, world, rank)]  # rows of A
     n0, n1 = w.n0, w.n1
     nl = n1 - n0
@@ -484,7 +495,8 @@ def make_e2e_step(a_h, b_h, w, peers, fused, world, rank, dev):
         sball = gather(sb.view(K, nl // BLOCK)).permute(1, 0, 2).reshape(-1)
         shim.codes = pb.view(K, nl)
         shim.scales = sball.view(kbn, N)[:, n0:n1].contiguous()
-        c = sharded_qgemm_fused(qa, shim, peers) if fused else sharded_qgemm(qa, shim)
+        c = ((sharded_qgemm_pull if pull else sharded_qgemm_fused)(qa, shim, peers) if fused
+             else sharded_qgemm(qa, shim))
         out_words.copy_(c._mx_packed.view(M, N // 2)[r0:r1].reshape(-1), non_blocking=True)
         out_scales.copy_(c._mx_scales.view(M, N // BLOCK)[r0:r1].reshape(-1), non_blocking=True)
         cur.synchronize()
@@ -793,8 +805,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true")
-    ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
-                    help="N > 1: output gather fused into the GEMM kernel, or NCCL all-gather")
+    ap.add_argument("--gather", default="fused", choices=["fused", "pull", "nccl"],
+                    help="N > 1: output gather fused into the GEMM kernel (peer stores), "
+                         "pulled by every SM after the local GEMM, or NCCL all-gather")
     ap.add_argument("--only", default=None, choices=["gemm", "gemm8192", "gemv1", "gemv16", "wo2048", "wo2048_fast", "quant",
                              "quant_f4", "dequant", "h",
                              "sweep"],

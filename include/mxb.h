@@ -275,6 +275,24 @@ int mxb_qgemm_sharded_sync(const void* a_packed, const float* a_scales, int64_t 
  */
 int mxb_peer_barrier(int nranks, int rank, void* const* sync_blocks, void* stream);
 
+/*
+ * Output all-gather of a column-sharded matmul, pulled by this rank: every
+ * peer's shard (columns col_off[r] .. col_off[r] + col_len[r] of every row)
+ * is read from out_words[r] / out_scales[r] (peer memory over NVLink, e.g.
+ * mxb_ipc_open mappings) into this rank's own out_words[rank] /
+ * out_scales[rank] by every SM (16-byte loads, several in flight); int16d
+ * codes [M][N_full] as 32-bit words, scales [M][N_full / 128].  The peers'
+ * shards must be complete before the launch (mxb_peer_barrier after their
+ * mxb_qgemm_sharded with only their own output), and a rank must not
+ * rewrite its shard while peers may still read it (alternate two output
+ * sets).  Offsets and widths multiples of 128, 1 <= nranks <= 8.  No
+ * counterpart in the reference (its matmul is single-device); the gather
+ * step of the N-sharded matmul.
+ */
+int mxb_allgather_cols(int nranks, int rank, int64_t M, int64_t N_full,
+                       const int64_t* col_off, const int64_t* col_len,
+                       void* const* out_words, float* const* out_scales, void* stream);
+
 /* Map a peer rank's device allocation into this process for the calling
  * thread's current device (cudaIpcOpenMemHandle with lazy peer access):
  * `handle` is the owner's cudaIpcMemHandle_t (handle_bytes == 64); *base

@@ -61,6 +61,7 @@ PROTOTYPES = {
                                       _int, _i64, _i64, _int, _int, _vp, _vp, _vp, _vp, _sz,
                                       _vp]),
     "mxb_peer_barrier": (_int, [_int, _int, _vp, _vp]),
+    "mxb_allgather_cols": (_int, [_int, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "mxb_ipc_open": (_int, [_vp, _i64, _vp]),
     "mxb_ipc_close": (_int, [_vp]),
     "mxb_linear_wonly_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int, _int, _int]),

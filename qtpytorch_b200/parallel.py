@@ -206,6 +206,48 @@ class PeerOutputs:
         self._opened = []
 
 
+def sharded_qgemm_pull(qa: mx_tensor, w: ShardedQGemmWeight, peers: PeerOutputs) -> mx_tensor:
+    """C = A @ B with B column-sharded, gathered by pulling: each rank's
+    GEMM writes its int16d tiles into its own full-width output only
+    (mxb_qgemm_sharded with one output), the device barrier orders the
+    ranks (mxb_peer_barrier), then every SM of each rank reads the peers'
+    shards over NVLink into its own output (mxb_allgather_cols).  Same
+    result as ``sharded_qgemm_fused``; no collective, graph-capturable."""
+    from . import _lib as L
+    import ctypes as C
+    M, K = qa._mx_orig_shape
+    if K != w.K:
+        raise ValueError("inner dimensions differ")
+    out_dt = optimal_output_dtype("matmul", qa._mx_dtype, w.dtype)
+    if out_dt.bits != 16:
+        raise NotImplementedError("the sharded gather writes int16d codes (int8 x int8)")
+    nl = w.n1 - w.n0
+    dev = qa._mx_packed.device
+    lib = L.load()
+    wsb = lib.mxb_qgemm_workspace_size(M, K, nl, w.dtype.bits, w.block)
+    ws = L.workspace(wsb, dev)
+    out = peers.next()
+    own_w = (C.c_void_p * 1)(out["ptr_w"][w.rank])
+    own_s = (C.c_void_p * 1)(out["ptr_s"][w.rank])
+    offs = (C.c_int64 * w.world)(*[a for a, _ in w.shards])
+    lens = (C.c_int64 * w.world)(*[b - a for a, b in w.shards])
+    with torch.cuda.device(dev):
+        rc = lib.mxb_qgemm_sharded(L.ptr(qa._mx_packed), L.ptr(qa._mx_scales),
+                                   qa._mx_scales.numel(), L.ptr(w.codes), L.ptr(w.scales),
+                                   w.scales.numel(), M, K, nl, w.dtype.bits, w.block, w.N,
+                                   w.n0, 1, C.cast(own_w, C.c_void_p), C.cast(own_s, C.c_void_p),
+                                   L.ptr(ws), wsb, L.stream_of(dev))
+        L.check(rc, f"mxb_qgemm_sharded({M}x{K}x{nl} of {w.N}, own output)")
+        if w.world > 1:
+            peers.barrier()
+            rc = lib.mxb_allgather_cols(w.world, w.rank, M, w.N, C.cast(offs, C.c_void_p),
+                                        C.cast(lens, C.c_void_p),
+                                        C.cast(out["ptr_w"], C.c_void_p),
+                                        C.cast(out["ptr_s"], C.c_void_p), L.stream_of(dev))
+            L.check(rc, "mxb_allgather_cols")
+    return mx_tensor(out["words"], out["scales"], out_dt, torch.Size([M, w.N]), M * w.N, w.block)
+
+
 def sharded_qgemm_fused(qa: mx_tensor, w: ShardedQGemmWeight, peers: PeerOutputs,
                         group=None, in_kernel_barrier: bool = True) -> mx_tensor:
     """C = A @ B with B column-sharded, the output all-gather fused into the

@@ -1,8 +1,8 @@
 """Worker of tests/test_gpu_dist.py, one process per GPU under torchrun:
 the column-sharded int8 matmul with the output gather fused into the
 kernel (peer stores), ordered by the in-kernel barrier or by an all-reduce
-after the launch, must equal, bit for bit, the NCCL-gather version and the
-single-GPU matmul.  Prints OK on rank 0."""
+after the launch, or pulled by every rank after its local matmul, must
+equal, bit for bit, the NCCL-gather version and the single-GPU matmul.  Prints OK on rank 0."""
 import os
 import sys
 
@@ -29,8 +29,11 @@ def main():
     peers = P.PeerOutputs(M, N, 128, world, rank, device=dev)
     ref_gather = P.sharded_qgemm(qa, w)
     full = qa @ qb
-    for it in range(6):  # both output sets, reuse, both barrier kinds
-        c = P.sharded_qgemm_fused(qa, w, peers, in_kernel_barrier=it < 4)
+    for it in range(9):  # both output sets, reuse, both barrier kinds, then pulled
+        if it < 6:
+            c = P.sharded_qgemm_fused(qa, w, peers, in_kernel_barrier=it < 4)
+        else:
+            c = P.sharded_qgemm_pull(qa, w, peers)
         torch.cuda.synchronize()
         assert torch.equal(c._mx_packed, ref_gather._mx_packed.view(torch.int32)), it
         assert torch.equal(c._mx_scales, ref_gather._mx_scales), it
