@@ -280,7 +280,7 @@ int mxb_peer_barrier(int nranks, int rank, void* const* sync_blocks, void* strea
  * peer's shard (columns col_off[r] .. col_off[r] + col_len[r] of every row)
  * is read from out_words[r] / out_scales[r] (peer memory over NVLink, e.g.
  * mxb_ipc_open mappings) into this rank's own out_words[rank] /
- * out_scales[rank] by every SM (16-byte loads, several in flight); int16d
+ * out_scales[rank] by every SM (16-byte loads, several in flight per thread); int16d
  * codes [M][N_full] as 32-bit words, scales [M][N_full / 128].  The peers'
  * shards must be complete before the launch (mxb_peer_barrier after their
  * mxb_qgemm_sharded with only their own output), and a rank must not

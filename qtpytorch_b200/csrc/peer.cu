@@ -21,7 +21,7 @@ struct ColShards {
 
 // Pull every peer's shard into this rank's output, the peers' memory read
 // over NVLink by every SM: each thread moves 16-byte chunks (8 codes of one
-// row), four loads in flight before their stores.  Chunk index i of peer r
+// row), eight loads in flight before their stores.  Chunk index i of peer r
 // is row i / (len / 8), chunk i % (len / 8).  Scales follow, one float per
 // 128 columns of a row.
 __global__ void __launch_bounds__(256) gather_cols_kernel(const __grid_constant__ ColShards g,
@@ -36,11 +36,11 @@ __global__ void __launch_bounds__(256) gather_cols_kernel(const __grid_constant_
     const int64_t per_row = g.len[r] / 8, c0 = g.off[r] / 8;
     const int64_t total = M * per_row;
     const uint4* src = g.words[r];
-    for (int64_t i = tid; i < total; i += 4 * nth) {
-      uint4 v[4];
-      int64_t at[4];
+    for (int64_t i = tid; i < total; i += 8 * nth) {
+      uint4 v[8];
+      int64_t at[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         const int64_t j = i + u * nth;
         at[u] = -1;
         if (j < total) {
@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(256) gather_cols_kernel(const __grid_constant_
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < 8; ++u)
         if (at[u] >= 0) out_words[at[u]] = v[u];
     }
     const int64_t sb = g.len[r] / 128, s0 = g.off[r] / 128, nsb = N_full / 128;
